@@ -1,0 +1,419 @@
+"""Benchmark of the paged decode path (one step = K1 append + K2 decode over the whole batch).
+
+Workload (the single-GPU configuration the headline metric is quoted on): one layer of paged
+decode at Llama-3-8B attention geometry — 32 query / 8 KV heads, head_dim 128, bf16,
+block_size 16, a pool of 65536 blocks — for 256 sequences whose context lengths are log-normal
+(median 1024, sigma 1.0, clipped to 16..8192), block tables drawn without replacement from a
+seeded permutation of the pool, Q/K/V ~ N(0,1)*0.5. Each step appends one K/V token per
+sequence through the slot mapping, then attends. Data is synthetic (seeded), and the ~1.7 GB
+of KV read per step is larger than L2, so no flush is needed between steps.
+
+``value`` = KV bytes read per step (sum(ctx) * 8 heads * 128 * 2 B * 2) / device step time,
+with inputs resident in HBM. ``e2e`` = the same bytes / step time through the C-ABI calls with
+pinned host buffers, H2D of the step's inputs and D2H of the attention output inside the timed
+region. ``roofline`` covers the decode kernel alone.
+
+Multi-GPU (torchrun): every rank runs its own seeded batch of 256 sequences (sequences are
+independent, so the path shards without any data-path collective; scaling is weak).
+
+``--impl reference`` times the CPU oracle (a restatement of transformers' eager attention over
+the gathered context, which is what tokenserve's HFBackend runs) on a bounded sample of the
+same workload, on the host cores.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "paged-attn decode KV-read GB/s (% of HBM peak); engine decode tokens/s"
+WORKLOAD = "paged decode op, Llama-3-8B attention (32q/8kv, D=128, bf16, block 16, pool 65536)"
+
+
+def parse() -> argparse.Namespace:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["cuda", "reference"], default="cuda")
+    ap.add_argument("--batch", type=int, default=256)
+    ap.add_argument("--cpu-sample-seconds", type=float, default=10.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def peaks() -> tuple[float, str]:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        return float(json.loads(p.read_text())["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def config(args: argparse.Namespace, n: int) -> dict:
+    return {
+        "workload": WORKLOAD,
+        "batch_per_gpu": args.batch,
+        "global_batch": args.batch * n,
+        "context": "log-normal median 1024 sigma 1.0 clipped 16..8192",
+        "l2": "inputs larger than L2 (~1.7 GB KV read per step), no flush",
+        "parallelism": f"independent sequence batches x{n}" if n > 1 else "single GPU",
+    }
+
+
+# ----------------------------------------------------------------------------- CPU side
+
+
+def cpu_sample(case, k_host, v_host, q_host, seqs, threads):  # type: ignore[no-untyped-def]
+    """One pass of the oracle over `seqs` (a bounded sample); returns seconds."""
+    import torch
+
+    from oracle.attention import eager_attention_torch
+
+    torch.set_num_threads(threads)
+    bs = case.block_size
+    t0 = time.perf_counter()
+    for i, b in enumerate(seqs):
+        ctx = int(case.context_lens[b])
+        nblk = (ctx + bs - 1) // bs
+        k = k_host[i][:, :nblk].reshape(case.num_kv_heads, nblk * bs, case.head_dim)[:, :ctx]
+        v = v_host[i][:, :nblk].reshape(case.num_kv_heads, nblk * bs, case.head_dim)[:, :ctx]
+        eager_attention_torch(q_host[i][:, None, :].float(), k.float(), v.float(),
+                              case.head_dim**-0.5, causal=False)  # fmt: skip
+    return time.perf_counter() - t0
+
+
+def gather_sample(case, kpool, vpool, q, budget_bytes):  # type: ignore[no-untyped-def]
+    """Copies the blocks of the first sequences (up to budget_bytes of KV) to the host."""
+    import torch
+
+    bs = case.block_size
+    seqs, used = [], 0
+    per_tok = case.num_kv_heads * case.head_dim * 2 * 2
+    for b in range(case.batch):
+        used += int(case.context_lens[b]) * per_tok
+        seqs.append(b)
+        if used >= budget_bytes:
+            break
+    ks, vs, qs = [], [], []
+    for b in seqs:
+        nblk = (int(case.context_lens[b]) + bs - 1) // bs
+        ids = torch.from_numpy(case.block_tables[b, :nblk].astype(np.int64)).to(kpool.device)
+        # [nblk, H, bs, D] -> [H, nblk, bs, D] (what the oracle's gather produces, per head)
+        ks.append(kpool.index_select(0, ids).transpose(0, 1).cpu())
+        vs.append(vpool.index_select(0, ids).transpose(0, 1).cpu())
+        qs.append(q[b].cpu())
+    return seqs, ks, vs, qs
+
+
+def cpu_rate(case, seqs, ks, vs, qs, seconds_target, threads):  # type: ignore[no-untyped-def]
+    """KV GB/s of the oracle on the sample, timed over repeats filling ~seconds_target."""
+    per_tok = case.num_kv_heads * case.head_dim * 2 * 2
+    sample_bytes = sum(int(case.context_lens[b]) for b in seqs) * per_tok
+    t1 = cpu_sample(case, ks, vs, qs, seqs, threads)
+    reps = max(1, int(seconds_target / max(t1, 1e-3)))
+    t = sum(cpu_sample(case, ks, vs, qs, seqs, threads) for _ in range(reps))
+    return sample_bytes * reps / t / 1e9, sample_bytes, reps
+
+
+# ----------------------------------------------------------------------------- clocks
+
+
+class ClockSampler:
+    FIELDS = (
+        "index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+        "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+        "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap"
+    )
+
+    def __init__(self, index: int) -> None:
+        self.index = index
+        self.proc = None
+
+    def __enter__(self) -> ClockSampler:
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True,
+            )  # fmt: skip
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc: object) -> None:
+        self.lines: list[str] = []
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                out, _ = self.proc.communicate()
+            self.lines = [ln for ln in out.splitlines() if ln.strip()]
+
+    def summary(self) -> dict | None:
+        rows = [[c.strip() for c in ln.split(",")] for ln in getattr(self, "lines", [])]
+        rows = [r for r in rows if len(r) >= 9]
+        if not rows:
+            return None
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = max((float(r[2]) for r in rows if r[2].replace(".", "").isdigit()), default=None)
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i] == "Active"})
+        return {
+            "sm_mhz": statistics.median(sm) if sm else None,
+            "sm_max_mhz": mx,
+            "reasons": reasons,
+            "samples": len(rows),
+        }
+
+
+# ----------------------------------------------------------------------------- main
+
+
+def main() -> None:
+    args = parse()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        if rank == 0:
+            run_reference(args, world)
+        return
+    run_cuda(args, world, rank, local)
+
+
+def run_reference(args: argparse.Namespace, world: int) -> None:
+    """CPU oracle on the box's host cores, on a bounded sample of each step's workload."""
+    import torch
+
+    from tokenserve_b200.workloads import decode_workload
+
+    case = decode_workload(seed=0, batch=args.batch)
+    threads = os.cpu_count() or 1
+    rng = np.random.default_rng(1)
+    # A sample of sequences whose KV fits a few seconds of CPU work; values seeded on the host.
+    per_tok = case.num_kv_heads * case.head_dim * 2 * 2
+    budget = 256 * 2**20
+    seqs, ks, vs, qs, used = [], [], [], [], 0
+    for b in range(case.batch):
+        ctx = int(case.context_lens[b])
+        nblk = (ctx + 15) // 16
+        shape = (case.num_kv_heads, nblk, 16, case.head_dim)
+        ks.append(torch.from_numpy((rng.standard_normal(shape) * 0.5).astype(np.float32)).bfloat16())
+        vs.append(torch.from_numpy((rng.standard_normal(shape) * 0.5).astype(np.float32)).bfloat16())
+        qs.append(torch.from_numpy((rng.standard_normal((case.num_q_heads, case.head_dim)) * 0.5).astype(np.float32)).bfloat16())
+        seqs.append(b)
+        used += ctx * per_tok
+        if used >= budget:
+            break
+    sample_bytes = sum(int(case.context_lens[b]) for b in seqs) * per_tok
+    for _ in range(args.warmup):
+        cpu_sample(case, ks, vs, qs, seqs, threads)
+    times = [cpu_sample(case, ks, vs, qs, seqs, threads) for _ in range(args.steps)]
+    total = sum(times)
+    gbs = sample_bytes * args.steps / total / 1e9
+    sample = f"{len(seqs)} of {case.batch} sequences ({sample_bytes / 1e6:.0f} MB of KV) per step"
+    print(json.dumps({
+        "impl": "reference",
+        "metric": METRIC,
+        "value": round(gbs, 3),
+        "unit": "GB/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(1000 * total / args.steps, 3),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f32 (bf16 inputs upcast, as HFBackend's float32 eager attention)",
+        "data": "synthetic",
+        "config": config(args, world),
+        "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": threads,
+                         "kind": "port", "sample": sample},
+        "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }))  # fmt: skip
+
+
+def run_cuda(args: argparse.Namespace, world: int, rank: int, local: int) -> None:
+    import torch
+    import torch.distributed as dist
+
+    from tokenserve_b200 import ops
+    from tokenserve_b200.workloads import decode_workload
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=dev)  # fmt: skip
+    ops.load_library()
+
+    case = decode_workload(seed=rank, batch=args.batch)
+    B, hq, hkv, d, bs = case.batch, case.num_q_heads, case.num_kv_heads, case.head_dim, 16
+    dt = torch.bfloat16
+    g = torch.Generator(device=dev).manual_seed(1000 + rank)
+    shape = (case.num_blocks, hkv, bs, d)
+    kpool = torch.empty(shape, dtype=dt, device=dev)
+    vpool = torch.empty(shape, dtype=dt, device=dev)
+    for p in (kpool, vpool):
+        for i in range(0, case.num_blocks, 8192):
+            p[i : i + 8192].normal_(0.0, 0.5, generator=g)
+    q = (torch.randn(B, hq, d, generator=g, device=dev) * 0.5).to(dt)
+    knew = (torch.randn(B, hkv, d, generator=g, device=dev) * 0.5).to(dt)
+    vnew = (torch.randn(B, hkv, d, generator=g, device=dev) * 0.5).to(dt)
+    slots = torch.from_numpy(case.append_slots).to(dev)
+    bt = torch.from_numpy(case.block_tables).to(dev)
+    cl = torch.from_numpy(case.context_lens).to(dev)
+    out = torch.empty(B, hq, d, dtype=dt, device=dev)
+    ws = torch.empty(ops.decode_workspace_size(B, hq, hkv, d, bt.shape[1], bs, dt),
+                     dtype=torch.uint8, device=dev)  # fmt: skip
+    scale = d**-0.5
+    kv_bytes = case.kv_bytes(2)
+    # Algorithmic bytes of one decode launch: KV read + q in + out + block-table entries.
+    blocks_read = int(((case.context_lens.astype(np.int64) + bs - 1) // bs).sum())
+    decode_bytes = kv_bytes + 2 * B * hq * d * 2 + blocks_read * 4 + B * 4
+    stream = torch.cuda.current_stream()
+
+    def step() -> None:
+        ops.reshape_and_cache(knew, vnew, kpool, vpool, slots)
+        ops.paged_decode(out, q, kpool, vpool, bt, cl, scale, ws)
+
+    def barrier() -> None:
+        if world > 1:
+            dist.barrier(device_ids=[local])
+        torch.cuda.synchronize()
+
+    # ---- device-resident timing
+    for _ in range(max(args.warmup, 3)):
+        step()
+    barrier()
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(2 * args.steps + 2)]
+    with ClockSampler(local) as clocks:
+        ev[0].record(stream)
+        for i in range(args.steps):
+            ops.reshape_and_cache(knew, vnew, kpool, vpool, slots)
+            ev[2 + 2 * i].record(stream)
+            ops.paged_decode(out, q, kpool, vpool, bt, cl, scale, ws)
+            ev[3 + 2 * i].record(stream)
+        ev[1].record(stream)
+        torch.cuda.synchronize()
+    barrier()
+    elapsed = ev[0].elapsed_time(ev[1]) / 1e3
+    dec_ms = [ev[2 + 2 * i].elapsed_time(ev[3 + 2 * i]) for i in range(args.steps)]
+    dec_avg = sum(dec_ms) / len(dec_ms) / 1e3
+
+    # ---- end to end through the C-ABI with host buffers
+    pin = lambda t: t.cpu().pin_memory()  # noqa: E731
+    h_q, h_k, h_v = pin(q), pin(knew), pin(vnew)
+    h_slots, h_bt, h_cl = pin(slots), pin(bt), pin(cl)
+    h_out = torch.empty(out.shape, dtype=dt).pin_memory()
+    d_q, d_k, d_v = torch.empty_like(q), torch.empty_like(knew), torch.empty_like(vnew)
+    d_slots, d_bt, d_cl = torch.empty_like(slots), torch.empty_like(bt), torch.empty_like(cl)
+    h2d = sum(t.numel() * t.element_size() for t in (h_q, h_k, h_v, h_slots, h_bt, h_cl))
+    d2h = h_out.numel() * h_out.element_size()
+
+    def e2e_step() -> None:
+        for dst, src in ((d_q, h_q), (d_k, h_k), (d_v, h_v), (d_slots, h_slots), (d_bt, h_bt),
+                         (d_cl, h_cl)):  # fmt: skip
+            dst.copy_(src, non_blocking=True)
+        ops.reshape_and_cache(d_k, d_v, kpool, vpool, d_slots)
+        ops.paged_decode(out, d_q, kpool, vpool, d_bt, d_cl, scale, ws)
+        h_out.copy_(out, non_blocking=True)
+        stream.synchronize()
+
+    for _ in range(max(args.warmup, 3)):
+        e2e_step()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    e2e_elapsed = e0.elapsed_time(e1) / 1e3
+
+    if world > 1:
+        t = torch.tensor([elapsed, e2e_elapsed], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        elapsed, e2e_elapsed = t.tolist()
+
+    if rank == 0:
+        peak, peak_kind = peaks()
+        achieved = decode_bytes / dec_avg / 1e9
+        value = world * kv_bytes * args.steps / elapsed / 1e9
+        line = {
+            "metric": METRIC,
+            "value": round(value, 2),
+            "unit": "GB/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": max(args.warmup, 3),
+            "ms_per_step": round(1000 * elapsed / args.steps, 4),
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "bf16",
+            "data": "synthetic",
+            "config": config(args, world),
+            "frac_of_hbm_peak": round(value / world / peak, 4),
+            "roofline": {
+                "bound": "hbm",
+                "kernel": "paged_decode_kernel",
+                "achieved": round(achieved, 1),
+                "peak": peak,
+                "peak_kind": peak_kind,
+                "unit": "GB/s",
+                "frac": round(achieved / peak, 4),
+                "traffic": None,
+                "algorithmic_bytes_per_launch": decode_bytes,
+                "avg_launch_us": round(dec_avg * 1e6, 2),
+            },
+            "e2e": {
+                "value": round(world * kv_bytes * args.steps / e2e_elapsed / 1e9, 2),
+                "unit": "GB/s",
+                "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h,
+                "ms_per_step": round(1000 * e2e_elapsed / args.steps, 4),
+            },
+            "gpu_launches": 3 * args.steps,
+            "clocks": clocks.summary(),
+        }
+        traffic = ROOT / "profiles" / "decode_traffic.json"
+        if traffic.exists():
+            tr = json.loads(traffic.read_text())
+            line["roofline"]["traffic"] = tr.get("bytes_per_full_launch")
+        if world == 1 and not args.no_cpu_baseline:
+            seqs, ks, vs, qs = gather_sample(case, kpool, vpool, q, 96 * 2**20)
+            threads = os.cpu_count() or 1
+            gbs, sb, reps = cpu_rate(case, seqs, ks, vs, qs, args.cpu_sample_seconds, threads)
+            line["cpu_baseline"] = {
+                "value": round(gbs, 3),
+                "unit": "GB/s",
+                "cores": threads,
+                "kind": "port",
+                "sample": f"{len(seqs)} of {B} sequences ({sb / 1e6:.0f} MB of KV) x {reps} passes",
+            }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier(device_ids=[local])
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

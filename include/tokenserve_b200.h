@@ -1,0 +1,177 @@
+/*
+ * tokenserve_b200 — C ABI of the B200 paged-KV execution kernels.
+ *
+ * These entry points are what a tokenserve `Backend` (src/tokenserve/backends/base.py:48-65)
+ * needs to execute one engine step on a paged KV cache. In the reference the same work is
+ * done by pure Python: the slot mapping and the shadow-KV write of SimulatedBackend
+ * (src/tokenserve/backends/base.py:40-45, src/tokenserve/backends/simulated.py:147-169) and
+ * the contiguous per-sequence attention of HFBackend (src/tokenserve/backends/hf.py:57-75,
+ * which runs transformers' eager_attention_forward). The reference binds no native code, so
+ * each function below names the Python code it replaces; the Python side binds them with
+ * ctypes (tokenserve_b200/ops.py).
+ *
+ * Conventions
+ *   - Every pointer argument is a DEVICE pointer unless its comment says otherwise. Tensors
+ *     stay owned by the caller; nothing here allocates device memory.
+ *   - `stream` is a cudaStream_t passed as void* (NULL = the legacy default stream). All work
+ *     is enqueued asynchronously on it; no call synchronises the device.
+ *   - Return value: 0 on success; a negative TS_ERR_* code when an argument is invalid
+ *     (nothing was launched); a positive cudaError_t when a launch failed. ts_last_error()
+ *     returns a message for the last failure on the calling thread.
+ *   - KV pool layout per layer: key_pool and value_pool are each
+ *     [num_blocks][num_kv_heads][block_size][head_dim] in `dtype`, contiguous. Physical slot
+ *     s = block_id * block_size + offset addresses row (s / block_size, h, s % block_size).
+ *   - Query head q uses KV head q / (num_q_heads / num_kv_heads) (grouped-query attention,
+ *     the head order of transformers' repeat_kv).
+ */
+#ifndef TOKENSERVE_B200_H
+#define TOKENSERVE_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define TS_ABI_VERSION 1
+
+/* Element types of queries, keys, values and attention outputs. */
+enum ts_dtype { TS_FLOAT32 = 0, TS_FLOAT16 = 1, TS_BFLOAT16 = 2 };
+
+/* Negative status codes (argument errors detected on the host before any launch). */
+enum ts_status {
+  TS_OK = 0,
+  TS_ERR_INVALID_ARGUMENT = -1,
+  TS_ERR_UNSUPPORTED = -2,
+  TS_ERR_WORKSPACE_TOO_SMALL = -3,
+  TS_ERR_MISALIGNED = -4,
+};
+
+/* ABI version of the loaded library (TS_ABI_VERSION it was built with). */
+int ts_version(void);
+
+/* Message for the most recent failing call on this thread ("" if none). Host pointer, valid
+ * until the next call on this thread. */
+const char* ts_last_error(void);
+
+/*
+ * K1 — write the KV of the step's new tokens into the paged pool (reshape_and_cache).
+ *
+ * Replaces: the slot mapping of BatchItem.slot_mapping (src/tokenserve/backends/base.py:40-45)
+ * and the write half of SimulatedBackend._write_and_verify
+ * (src/tokenserve/backends/simulated.py:156-160), here carrying real K/V rows instead of
+ * token ids.
+ *
+ * key, value:   [num_tokens][num_kv_heads][head_dim] in dtype; token t's row starts at
+ *               key + t * key_token_stride elements (heads contiguous, stride head_dim).
+ * slot_mapping: [num_tokens] int64; slot < 0 skips the token (padding).
+ * token_tags:   optional int32 [num_tokens] (NULL = off); when set, tag_pool (int32
+ *               [num_blocks * block_size]) receives token_tags[t] at slot_mapping[t]. This is
+ *               the device shadow of SimulatedBackend's shadow array (simulated.py:101).
+ * error_flag:   optional int32 device word (NULL = off). A slot >= num_blocks * block_size is
+ *               skipped and sets *error_flag to 1; nothing outside the pool is written.
+ */
+int ts_reshape_and_cache(const void* key, const void* value, int64_t key_token_stride,
+                         int64_t value_token_stride, void* key_pool, void* value_pool,
+                         const int64_t* slot_mapping, int64_t num_tokens, int32_t num_kv_heads,
+                         int32_t head_dim, int32_t block_size, int64_t num_blocks, int32_t dtype,
+                         const int32_t* token_tags, int32_t* tag_pool, int32_t* error_flag,
+                         void* stream);
+
+/* Bytes of device workspace ts_paged_decode needs for these sizes (0 is possible). */
+size_t ts_paged_decode_workspace_size(int32_t batch, int32_t num_q_heads, int32_t num_kv_heads,
+                                      int32_t head_dim, int32_t max_blocks_per_seq,
+                                      int32_t block_size, int32_t dtype);
+
+/*
+ * K2 — paged decode attention: one query token per sequence attends to its whole context.
+ *
+ * Replaces: transformers 5.5.0 eager_attention_forward (models/llama/modeling_llama.py:199,
+ * with repeat_kv :187) as called by HFBackend._execute (src/tokenserve/backends/hf.py:71)
+ * for a decode step, over a contiguous per-sequence cache.
+ *
+ * out:          [batch][num_q_heads][head_dim] in dtype, contiguous.
+ * query:        [batch][num_q_heads][head_dim]; sequence b's row starts at
+ *               query + b * query_token_stride elements.
+ * block_tables: int32 [batch][max_blocks_per_seq] (row-major); entries past the context are
+ *               ignored.
+ * context_lens: int32 [batch]; tokens 0..context_lens[b]-1 (the new token included) are
+ *               attended. 0 writes zeros.
+ * scale:        softmax scale (head_dim ** -0.5 for Llama).
+ * workspace:    device scratch of at least ts_paged_decode_workspace_size(...) bytes. Its
+ *               first 4096 bytes must be zero before the first call (they are left zero
+ *               after every completed call).
+ */
+int ts_paged_decode(void* out, const void* query, int64_t query_token_stride,
+                    const void* key_pool, const void* value_pool, const int32_t* block_tables,
+                    int32_t max_blocks_per_seq, const int32_t* context_lens, int32_t batch,
+                    int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim,
+                    int32_t block_size, int64_t num_blocks, float scale, int32_t dtype,
+                    void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * K3 — paged chunked-prefill attention (causal): each sequence's new chunk of queries
+ * attends to its cached prefix blocks plus the chunk itself, all read through the block
+ * table (the chunk's K/V must already be in the pool, written by ts_reshape_and_cache).
+ *
+ * Replaces: the same eager_attention_forward path for a multi-token step with a causal mask
+ * (HFBackend recomputes from position 0 when it holds no cache, hf.py:62-65; here the
+ * cached prefix is reused).
+ *
+ * out, query:      [num_query_tokens][num_q_heads][head_dim]; query token i of the batch
+ *                  starts at query + i * query_token_stride elements; out is contiguous.
+ * query_start_loc: int32 [num_seqs + 1]; sequence s owns query rows
+ *                  query_start_loc[s] .. query_start_loc[s+1]-1.
+ * context_lens:    int32 [num_seqs]; total tokens of sequence s after this step. Query row j
+ *                  of sequence s sits at position context_lens[s] - q_len + j and attends to
+ *                  positions 0..that position.
+ * max_query_len:   an upper bound of the per-sequence query lengths.
+ */
+int ts_paged_prefill(void* out, const void* query, int64_t query_token_stride,
+                     const void* key_pool, const void* value_pool, const int32_t* block_tables,
+                     int32_t max_blocks_per_seq, const int32_t* query_start_loc,
+                     const int32_t* context_lens, int32_t num_seqs, int32_t num_query_tokens,
+                     int32_t max_query_len, int32_t num_q_heads, int32_t num_kv_heads,
+                     int32_t head_dim, int32_t block_size, int64_t num_blocks, float scale,
+                     int32_t dtype, void* stream);
+
+/*
+ * K4 — batched block copy (preemption swap-in / copy-on-write).
+ *
+ * Replaces: nothing in the reference, which preempts by recompute
+ * (src/tokenserve/scheduler.py:215-225) and shares only full blocks
+ * (src/tokenserve/kv_cache.py:179-199); it is validated against an index copy.
+ *
+ * pool_base:          start of num_planes equally sized planes (e.g. [layers][2] pools).
+ * plane_stride_bytes: distance between planes; block b of plane p starts at
+ *                     pool_base + p * plane_stride_bytes + b * block_bytes.
+ * src_dst:            int64 [num_pairs][2] of (source block, destination block). Sources
+ *                     and destinations must be disjoint sets.
+ * num_blocks:         blocks per plane (for bounds checking); an out-of-range pair is
+ *                     skipped and sets *error_flag (optional, may be NULL).
+ */
+int ts_copy_blocks(void* pool_base, int64_t num_planes, int64_t plane_stride_bytes,
+                   int64_t block_bytes, int64_t num_blocks, const int64_t* src_dst,
+                   int64_t num_pairs, int32_t* error_flag, void* stream);
+
+/*
+ * Shadow-KV verification of the token tags written by ts_reshape_and_cache: for each
+ * sequence, every position 0..context_lens[b]-1 read back through its block table must hold
+ * expected_tokens (concatenated per sequence at expected_offsets[b]). The first mismatch per
+ * sequence is reported in mismatch_pos[b] (-1 = none; host reads it after the stream syncs).
+ *
+ * Replaces: the read half of SimulatedBackend._write_and_verify
+ * (src/tokenserve/backends/simulated.py:161-169).
+ */
+int ts_verify_tags(const int32_t* tag_pool, const int32_t* block_tables,
+                   int32_t max_blocks_per_seq, const int32_t* context_lens,
+                   const int64_t* expected_offsets, const int32_t* expected_tokens,
+                   int32_t batch, int32_t block_size, int64_t num_blocks,
+                   int32_t* mismatch_pos, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* TOKENSERVE_B200_H */

@@ -1,0 +1,168 @@
+"""``CudaPagedBackend`` — a drop-in tokenserve ``Backend`` that executes on a B200.
+
+It plugs into tokenserve exactly where ``HFBackend`` does (src/tokenserve/backends/hf.py:36-90):
+``Engine.step`` awaits ``backend.execute(batch)`` (src/tokenserve/engine.py:311) with the
+``BatchItem`` list built from the scheduler's decisions and the KVCacheManager's block tables,
+and gets back ``seq_id -> sampled token`` for the items with ``sample`` set.
+
+Unlike ``HFBackend`` it keeps a real paged KV cache on the device, indexed by the very block
+ids KVCacheManager hands out, so it supports prefix caching (a prefix-cache hit reads blocks
+another sequence computed) and ``free`` has nothing to release: blocks belong to the manager.
+
+Threading and ordering follow tokenserve's contract: ``execute`` runs in a worker thread
+(``asyncio.to_thread``, as hf.py:50-52 does) and returns only after the sampled ids are back on
+the host, so all device reads and writes of the pool have finished before the engine mutates
+the block tables again (engine.py:1-13).
+"""
+
+from __future__ import annotations
+
+import asyncio
+from collections.abc import Sequence as Seq
+from dataclasses import dataclass
+
+import numpy as np
+import torch
+
+from tokenserve_b200 import ops
+from tokenserve_b200.interface import Backend, BatchItem, KVCorruptionError
+from tokenserve_b200.model import PagedLlamaRunner
+from tokenserve_b200.step import plan_step
+
+
+@dataclass(frozen=True, slots=True)
+class CudaPagedBackendConfig:
+    """Must match the engine's ``EngineConfig.block_size`` / ``num_blocks`` (engine.py:42-57)."""
+
+    block_size: int = 16
+    num_blocks: int = 2048
+    device: str = "cuda"
+    #: KV-cache and compute dtype; ``None`` keeps the model's dtype.
+    dtype: torch.dtype | None = None
+    #: Keep a device shadow of the token id in every KV slot and check each sequence's whole
+    #: context every step, like SimulatedBackend(verify_kv=True) (simulated.py:86-92, 147-169).
+    verify_kv: bool = False
+
+    def __post_init__(self) -> None:
+        if self.block_size <= 0 or self.num_blocks <= 0:
+            raise ValueError("block_size and num_blocks must be positive")
+
+
+def sample_token(logits: torch.Tensor, item: BatchItem) -> int:
+    """tokenserve's sampling rule (src/tokenserve/backends/hf.py:78-90) on one logits row.
+
+    Greedy is an argmax; otherwise temperature and top-p on the host with a CPU generator
+    seeded by ``(seed * 1_000_003 + output_index)``, so a recomputed sequence samples the same
+    tokens.
+    """
+    if item.temperature <= 0.0:
+        return int(torch.argmax(logits).item())
+    probs = torch.softmax(logits.float().cpu() / item.temperature, dim=-1)
+    if item.top_p < 1.0:
+        sorted_probs, order = torch.sort(probs, descending=True)
+        outside = torch.cumsum(sorted_probs, dim=-1) - sorted_probs > item.top_p
+        sorted_probs[outside] = 0.0
+        probs = torch.zeros_like(probs).scatter_(0, order, sorted_probs)
+    gen = torch.Generator(device="cpu")
+    gen.manual_seed((item.seed * 1_000_003 + item.output_index) & 0x7FFF_FFFF_FFFF_FFFF)
+    return int(torch.multinomial(probs, 1, generator=gen).item())
+
+
+class CudaPagedBackend(Backend):
+    name = "cuda-paged"
+    supports_prefix_caching = True
+
+    def __init__(self, model: torch.nn.Module, config: CudaPagedBackendConfig) -> None:
+        if not torch.cuda.is_available():
+            raise RuntimeError("CudaPagedBackend needs a CUDA device (there is no CPU fallback)")
+        ops.load_library()
+        self.config = config
+        self.device = torch.device(config.device)
+        if self.device.index is None:
+            self.device = torch.device("cuda", torch.cuda.current_device())
+        with torch.cuda.device(self.device):
+            self.runner = PagedLlamaRunner(
+                model,
+                num_blocks=config.num_blocks,
+                block_size=config.block_size,
+                device=self.device,
+                dtype=config.dtype,
+            )
+            self._tags = (
+                torch.full((config.num_blocks * config.block_size,), -1, dtype=torch.int32,
+                           device=self.device)
+                if config.verify_kv else None
+            )  # fmt: skip
+            self.runner.tag_pool = self._tags
+        self.num_steps = 0
+        self.num_tokens = 0
+
+    @property
+    def max_position_embeddings(self) -> int | None:
+        return getattr(self.runner.model.config, "max_position_embeddings", None)
+
+    async def execute(self, batch: Seq[BatchItem]) -> dict[int, int]:
+        # Device work is synchronous from the engine's point of view; keep it off the loop.
+        return await asyncio.to_thread(self._execute, list(batch))
+
+    def free(self, seq_id: int) -> None:
+        """Nothing to drop: KV blocks are owned and recycled by tokenserve's KVCacheManager."""
+
+    async def close(self) -> None:
+        self.runner.kv = torch.empty(0, device=self.device)
+        self._tags = self.runner.tag_pool = None
+        torch.cuda.empty_cache()
+
+    def _execute(self, batch: list[BatchItem]) -> dict[int, int]:
+        if not batch:
+            return {}
+        cfg = self.config
+        plan = plan_step(batch, cfg.block_size, cfg.num_blocks)
+        with torch.cuda.device(self.device), torch.inference_mode():
+            st = self.runner.upload(plan)
+            logits = self.runner.forward(st)
+            if self._tags is not None:
+                self._verify_tags(batch)
+            sampled: dict[int, int] = {}
+            if logits.shape[0]:
+                greedy = torch.argmax(logits, dim=-1).cpu().numpy()
+                for r, item in enumerate(plan.sample_items):
+                    if item.temperature <= 0.0:
+                        sampled[item.seq_id] = int(greedy[r])
+                    else:
+                        sampled[item.seq_id] = sample_token(logits[r], item)
+            else:
+                torch.cuda.current_stream().synchronize()
+        self.num_steps += 1
+        self.num_tokens += plan.num_tokens
+        return sampled
+
+    # ------------------------------------------------------------ shadow-KV verification
+
+    def _verify_tags(self, batch: list[BatchItem]) -> None:
+        """Reads every sequence's context back through its table (simulated.py:161-169)."""
+        bs = self.config.block_size
+        n = len(batch)
+        width = max(len(it.block_table) for it in batch)
+        tables = np.zeros((n, width), dtype=np.int32)
+        for i, it in enumerate(batch):
+            tables[i, : len(it.block_table)] = it.block_table
+        ctx = np.array([it.end for it in batch], dtype=np.int32)
+        offs = np.zeros(n, dtype=np.int64)
+        offs[1:] = np.cumsum(ctx[:-1])
+        toks = np.concatenate([np.asarray(it.token_ids[: it.end], dtype=np.int32) for it in batch])
+        dev = [torch.from_numpy(a).to(self.device) for a in (tables, ctx, offs, toks)]
+        bad = torch.empty(n, dtype=torch.int32, device=self.device)
+        ops.verify_tags(self._tags, dev[0], dev[1], dev[2], dev[3], bs, bad)
+        bad_h = bad.cpu().numpy()
+        shadow = None
+        for i, it in enumerate(batch):
+            pos = int(bad_h[i])
+            if pos >= 0:
+                if shadow is None:
+                    shadow = self._tags.cpu().numpy()
+                got = int(shadow[tables[i, pos // bs] * bs + pos % bs])
+                raise KVCorruptionError(
+                    f"seq {it.seq_id} position {pos}: KV slot holds token {got}, "
+                    f"expected {it.token_ids[pos]}"
+                )

@@ -1,0 +1,179 @@
+"""Paged execution of a Hugging Face Llama model on one B200.
+
+The dense parts of the layer (RMSNorm, Q/K/V/O projections, rotary embedding, SwiGLU MLP,
+final norm and lm_head) run as the model's own torch modules (cuBLAS GEMMs); attention and the
+KV cache are the hand-written kernels: K1 writes the step's K/V rows into the block pool, K2
+attends the decode rows and K3 the chunked-prefill rows, all through the block tables that
+tokenserve's KVCacheManager produced. The per-layer math is the one of transformers 5.5.0
+``LlamaDecoderLayer`` / ``LlamaAttention.forward`` (models/llama/modeling_llama.py:225-290),
+which HFBackend runs per sequence (src/tokenserve/backends/hf.py:71).
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import numpy as np
+import torch
+
+from tokenserve_b200 import ops
+from tokenserve_b200.step import StepPlan
+
+
+def _rope(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.Tensor:
+    """``x * cos + rotate_half(x) * sin`` on ``[T, H, D]`` with ``cos/sin [T, D]``."""
+    half = x.shape[-1] // 2
+    rot = torch.cat((-x[..., half:], x[..., :half]), dim=-1)
+    return x * cos[:, None, :] + rot * sin[:, None, :]
+
+
+@dataclass
+class DeviceStep:
+    """A StepPlan uploaded to the device (views into one staging copy)."""
+
+    input_ids: torch.Tensor
+    positions: torch.Tensor
+    slot_mapping: torch.Tensor
+    decode_tables: torch.Tensor
+    decode_ctx: torch.Tensor
+    prefill_tables: torch.Tensor
+    prefill_qsl: torch.Tensor
+    prefill_ctx: torch.Tensor
+    sample_rows: torch.Tensor
+    tags: torch.Tensor  # int32 token ids of the new slots (shadow-KV check)
+    num_decode: int
+    num_prefill: int
+    max_query_len: int
+
+
+class Staging:
+    """Pinned host buffer + device buffer; one H2D copy per step for all metadata."""
+
+    def __init__(self, device: torch.device) -> None:
+        self.device = device
+        self.host = torch.empty(0, dtype=torch.uint8).pin_memory()
+        self.dev = torch.empty(0, dtype=torch.uint8, device=device)
+
+    def upload(self, arrays: list[np.ndarray]) -> list[torch.Tensor]:
+        sizes = [(a.nbytes + 255) // 256 * 256 for a in arrays]
+        total = max(256, sum(sizes))
+        if self.host.numel() < total:
+            cap = max(total, 2 * self.host.numel())
+            self.host = torch.empty(cap, dtype=torch.uint8).pin_memory()
+            self.dev = torch.empty(cap, dtype=torch.uint8, device=self.device)
+        hv = self.host.numpy()
+        off = 0
+        spans = []
+        for a, sz in zip(arrays, sizes, strict=True):
+            hv[off : off + a.nbytes] = np.ascontiguousarray(a).view(np.uint8).reshape(-1)
+            spans.append((off, a))
+            off += sz
+        self.dev[:off].copy_(self.host[:off], non_blocking=True)
+        out = []
+        for o, a in spans:
+            t = self.dev[o : o + a.nbytes].view(torch.from_numpy(a[:0]).dtype)
+            out.append(t.view(a.shape))
+        return out
+
+
+class PagedLlamaRunner:
+    """Runs steps of a ``LlamaForCausalLM`` against a device-resident paged KV pool."""
+
+    def __init__(
+        self,
+        model: torch.nn.Module,
+        *,
+        num_blocks: int,
+        block_size: int,
+        device: torch.device | str = "cuda",
+        dtype: torch.dtype | None = None,
+    ) -> None:
+        self.device = torch.device(device)
+        self.model = model.to(self.device).eval()
+        cfg = model.config
+        self.dtype = dtype or next(model.parameters()).dtype
+        if self.dtype != next(model.parameters()).dtype:
+            self.model = self.model.to(self.dtype)
+        self.num_layers = cfg.num_hidden_layers
+        self.num_q_heads = cfg.num_attention_heads
+        self.num_kv_heads = cfg.num_key_value_heads
+        self.head_dim = getattr(cfg, "head_dim", None) or cfg.hidden_size // cfg.num_attention_heads
+        self.scale = self.head_dim**-0.5
+        self.block_size = block_size
+        self.num_blocks = num_blocks
+        # [layer][K|V][block][kv head][slot in block][head_dim]
+        self.kv = torch.zeros(
+            (self.num_layers, 2, num_blocks, self.num_kv_heads, block_size, self.head_dim),
+            dtype=self.dtype,
+            device=self.device,
+        )
+        self.staging = Staging(self.device)
+        self._ws = torch.empty(0, dtype=torch.uint8, device=self.device)
+        self.base = self.model.model
+        self.rotary = self.base.rotary_emb
+        #: int32 [num_blocks * block_size] token id per slot, or None (shadow-KV check off)
+        self.tag_pool: torch.Tensor | None = None
+
+    def workspace(self, batch: int, max_blocks: int) -> torch.Tensor | None:
+        n = ops.decode_workspace_size(
+            batch, self.num_q_heads, self.num_kv_heads, self.head_dim, max_blocks,
+            self.block_size, self.dtype,
+        )  # fmt: skip
+        if n == 0:
+            return None
+        if self._ws.numel() < n:
+            self._ws = torch.empty(n, dtype=torch.uint8, device=self.device)
+        return self._ws
+
+    def upload(self, plan: StepPlan) -> DeviceStep:
+        tags = plan.input_ids.astype(np.int32) if self.tag_pool is not None else np.empty(0, np.int32)
+        (ids, pos, slots, dtab, dctx, ptab, pqsl, pctx, srows, tg) = self.staging.upload(
+            [
+                plan.input_ids, plan.positions, plan.slot_mapping, plan.decode_tables,
+                plan.decode_ctx, plan.prefill_tables, plan.prefill_qsl, plan.prefill_ctx,
+                plan.sample_rows, tags,
+            ]
+        )  # fmt: skip
+        return DeviceStep(
+            ids, pos, slots, dtab, dctx, ptab, pqsl, pctx, srows, tg, plan.num_decode,
+            plan.num_prefill, plan.max_query_len,
+        )  # fmt: skip
+
+    def attention(self, layer: int, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
+                  st: DeviceStep) -> torch.Tensor:  # fmt: skip
+        kp, vp = self.kv[layer, 0], self.kv[layer, 1]
+        tagged = layer == 0 and self.tag_pool is not None
+        ops.reshape_and_cache(
+            k, v, kp, vp, st.slot_mapping,
+            token_tags=st.tags if tagged else None, tag_pool=self.tag_pool if tagged else None,
+        )  # fmt: skip
+        out = torch.empty(q.shape, dtype=q.dtype, device=q.device)
+        nd = st.num_decode
+        if nd:
+            ws = self.workspace(nd, st.decode_tables.shape[1])
+            ops.paged_decode(out[:nd], q[:nd], kp, vp, st.decode_tables, st.decode_ctx,
+                             self.scale, ws)  # fmt: skip
+        if st.num_prefill:
+            ops.paged_prefill(out[nd:], q[nd:], kp, vp, st.prefill_tables, st.prefill_qsl,
+                              st.prefill_ctx, st.max_query_len, self.scale)  # fmt: skip
+        return out
+
+    @torch.inference_mode()
+    def forward(self, st: DeviceStep) -> torch.Tensor:
+        """Runs every layer over the step's tokens; returns float32 logits of the sampled rows."""
+        h = self.base.embed_tokens(st.input_ids)
+        cos, sin = self.rotary(h, st.positions[None, :])
+        cos, sin = cos[0], sin[0]
+        t = h.shape[0]
+        hq, hkv, d = self.num_q_heads, self.num_kv_heads, self.head_dim
+        for li, layer in enumerate(self.base.layers):
+            attn = layer.self_attn
+            x = layer.input_layernorm(h)
+            q = _rope(attn.q_proj(x).view(t, hq, d), cos, sin)
+            k = _rope(attn.k_proj(x).view(t, hkv, d), cos, sin)
+            v = attn.v_proj(x).view(t, hkv, d)
+            o = self.attention(li, q, k, v, st)
+            h = h + attn.o_proj(o.view(t, hq * d))
+            h = h + layer.mlp(layer.post_attention_layernorm(h))
+        hs = self.base.norm(h[st.sample_rows])
+        return self.model.lm_head(hs).float()

@@ -1,0 +1,95 @@
+"""Seeded synthetic paged-KV workloads with the shapes of the benchmarked configurations.
+
+* :func:`decode_workload` — single-layer paged decode at Llama-3-8B attention geometry
+  (32 query / 8 KV heads, head_dim 128, bf16, block_size 16, a pool of 65536 blocks), a batch of
+  256 sequences with log-normal context lengths (median 1024, sigma 1.0, clipped to 16..8192),
+  block tables drawn without replacement from a seeded permutation of the pool, and Q/K/V
+  ~ N(0, 1) * 0.5. Each step appends one K/V token per sequence, then attends.
+* :func:`small_paged_case` — the same construction at sizes a CPU oracle checks in seconds.
+
+Only numpy is used for the index arithmetic, so the same seed gives the same tables on every
+machine.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import numpy as np
+
+
+@dataclass
+class PagedCase:
+    num_blocks: int
+    block_size: int
+    num_q_heads: int
+    num_kv_heads: int
+    head_dim: int
+    context_lens: np.ndarray  # int32 [B], including the token appended this step
+    block_tables: np.ndarray  # int32 [B, max_blocks], padded with 0
+    seed: int
+
+    @property
+    def batch(self) -> int:
+        return int(self.context_lens.shape[0])
+
+    @property
+    def append_slots(self) -> np.ndarray:
+        """int64 [B] slot of each sequence's newest token (position ctx - 1)."""
+        pos = self.context_lens.astype(np.int64) - 1
+        blk = self.block_tables[np.arange(self.batch), pos // self.block_size].astype(np.int64)
+        return blk * self.block_size + pos % self.block_size
+
+    def kv_bytes(self, elem_size: int) -> int:
+        """Algorithmic K+V bytes one decode pass reads: sum(ctx) * Hkv * D * elem * 2."""
+        return int(self.context_lens.astype(np.int64).sum()) * self.num_kv_heads * self.head_dim * elem_size * 2
+
+
+def lognormal_context_lens(
+    rng: np.random.Generator, batch: int, median: float, sigma: float, lo: int, hi: int
+) -> np.ndarray:
+    z = rng.standard_normal(batch)
+    return np.clip(np.round(np.exp(np.log(median) + sigma * z)), lo, hi).astype(np.int32)
+
+
+def tables_from_permutation(
+    rng: np.random.Generator, context_lens: np.ndarray, num_blocks: int, block_size: int
+) -> np.ndarray:
+    """Each sequence's blocks drawn without replacement from one permutation of the pool."""
+    need = (context_lens.astype(np.int64) + block_size - 1) // block_size
+    if need.sum() > num_blocks:
+        raise ValueError(f"workload needs {need.sum()} blocks, pool has {num_blocks}")
+    perm = rng.permutation(num_blocks).astype(np.int32)
+    width = int(need.max())
+    tables = np.zeros((len(context_lens), width), dtype=np.int32)
+    off = 0
+    for b, n in enumerate(need.tolist()):
+        tables[b, :n] = perm[off : off + n]
+        off += n
+    return tables
+
+
+def decode_workload(seed: int = 0, batch: int = 256, num_blocks: int = 65536) -> PagedCase:
+    """The Llama-3-8B decode-op workload (see module docstring)."""
+    rng = np.random.default_rng(seed)
+    ctx = lognormal_context_lens(rng, batch, 1024.0, 1.0, 16, 8192)
+    tables = tables_from_permutation(rng, ctx, num_blocks, 16)
+    return PagedCase(num_blocks, 16, 32, 8, 128, ctx, tables, seed)
+
+
+def small_paged_case(
+    seed: int,
+    context_lens: list[int],
+    *,
+    num_q_heads: int = 8,
+    num_kv_heads: int = 2,
+    head_dim: int = 128,
+    block_size: int = 16,
+    spare_blocks: int = 8,
+) -> PagedCase:
+    rng = np.random.default_rng(seed)
+    ctx = np.asarray(context_lens, dtype=np.int32)
+    need = int(((ctx.astype(np.int64) + block_size - 1) // block_size).sum())
+    nb = need + spare_blocks
+    tables = tables_from_permutation(rng, ctx, nb, block_size)
+    return PagedCase(nb, block_size, num_q_heads, num_kv_heads, head_dim, ctx, tables, seed)
