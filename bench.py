@@ -27,7 +27,6 @@ import argparse
 import json
 import os
 import statistics
-import subprocess
 import sys
 import time
 from pathlib import Path
@@ -50,6 +49,8 @@ def parse() -> argparse.Namespace:
     ap.add_argument("--batch", type=int, default=256)
     ap.add_argument("--cpu-sample-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--pool-blocks", type=int, default=65536)
+    ap.add_argument("--skip-e2e", action="store_true", help="profiling runs only")
     return ap.parse_args()
 
 
@@ -58,6 +59,26 @@ def peaks() -> tuple[float, str]:
     if p.exists():
         return float(json.loads(p.read_text())["hbm_gbs"]), "measured"
     return 6650.0, "fallback"
+
+
+def measured_traffic(decode_bytes: int) -> int | None:
+    """DRAM bytes per full-size decode launch from the committed ncu summary, if present.
+
+    The summary records dram__bytes_read.sum + dram__bytes_write.sum of one captured launch
+    and that launch's algorithmic bytes; traffic grows with the KV read, so it is scaled to
+    this workload's algorithmic bytes.
+    """
+    p = ROOT / "profiles" / "paged_decode_llama8b.md"
+    if not p.exists():
+        return None
+    vals = {}
+    for ln in p.read_text().splitlines():
+        if ln.startswith("traffic_bytes:") or ln.startswith("algorithmic_bytes:"):
+            k, v = ln.split(":", 1)
+            vals[k] = float(v.strip())
+    if len(vals) < 2:
+        return None
+    return int(vals["traffic_bytes"] / vals["algorithmic_bytes"] * decode_bytes)
 
 
 def config(args: argparse.Namespace, n: int) -> dict:
@@ -130,52 +151,87 @@ def cpu_rate(case, seqs, ks, vs, qs, seconds_target, threads):  # type: ignore[n
 
 
 class ClockSampler:
-    FIELDS = (
-        "index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-        "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-        "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap"
-    )
+    """Polls SM clock, power and clock-event reasons through NVML while the timed region runs.
 
-    def __init__(self, index: int) -> None:
-        self.index = index
-        self.proc = None
+    Read-only NVML queries (no setting is changed). The thread keeps sampling until the
+    context exits, which the caller places after the device synchronisation that ends the
+    timed region.
+    """
+
+    REASONS = {
+        "hw_slowdown": 0x8,
+        "sw_thermal_slowdown": 0x20,
+        "hw_thermal_slowdown": 0x40,
+        "sw_power_cap": 0x4,
+    }
+
+    def __init__(self, device) -> None:  # type: ignore[no-untyped-def]
+        self.device = device
+        self.samples: list[tuple[float, float, int]] = []
+        self.max_mhz: float | None = None
+        self._stop = False
+        self._thread = None
+
+    def _handle(self):  # type: ignore[no-untyped-def]
+        import pynvml
+        import torch
+
+        pynvml.nvmlInit()
+        props = torch.cuda.get_device_properties(self.device)
+        bus = getattr(props, "pci_bus_id", None)
+        if bus is not None:
+            dom = getattr(props, "pci_domain_id", 0)
+            devid = getattr(props, "pci_device_id", 0)
+            try:
+                return pynvml.nvmlDeviceGetHandleByPciBusId(f"{dom:08x}:{bus:02x}:{devid:02x}.0")
+            except pynvml.NVMLError:
+                pass
+        return pynvml.nvmlDeviceGetHandleByIndex(self.device.index or 0)
+
+    def _run(self, h) -> None:  # type: ignore[no-untyped-def]
+        import pynvml
+
+        while not self._stop:
+            try:
+                sm = pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM)
+                pw = pynvml.nvmlDeviceGetPowerUsage(h) / 1000.0
+                rs = pynvml.nvmlDeviceGetCurrentClocksEventReasons(h)
+                self.samples.append((float(sm), pw, int(rs)))
+            except Exception:  # noqa: BLE001 - sampling is best effort
+                return
+            time.sleep(0.001)
 
     def __enter__(self) -> ClockSampler:
+        import threading
+
         try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}",
-                 "--format=csv,noheader,nounits", "-lms", "200"],
-                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True,
-            )  # fmt: skip
-        except OSError:
-            self.proc = None
+            import pynvml
+
+            h = self._handle()
+            self.max_mhz = float(pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM))
+            self._thread = threading.Thread(target=self._run, args=(h,), daemon=True)
+            self._thread.start()
+        except Exception:  # noqa: BLE001
+            self._thread = None
         return self
 
     def __exit__(self, *exc: object) -> None:
-        self.lines: list[str] = []
-        if self.proc is not None:
-            self.proc.terminate()
-            try:
-                out, _ = self.proc.communicate(timeout=5)
-            except subprocess.TimeoutExpired:
-                self.proc.kill()
-                out, _ = self.proc.communicate()
-            self.lines = [ln for ln in out.splitlines() if ln.strip()]
+        self._stop = True
+        if self._thread is not None:
+            self._thread.join(timeout=5)
 
     def summary(self) -> dict | None:
-        rows = [[c.strip() for c in ln.split(",")] for ln in getattr(self, "lines", [])]
-        rows = [r for r in rows if len(r) >= 9]
-        if not rows:
+        if not self.samples:
             return None
-        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
-        mx = max((float(r[2]) for r in rows if r[2].replace(".", "").isdigit()), default=None)
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i] == "Active"})
+        reasons = sorted({n for _, _, r in self.samples for n, bit in self.REASONS.items()
+                          if r & bit})  # fmt: skip
         return {
-            "sm_mhz": statistics.median(sm) if sm else None,
-            "sm_max_mhz": mx,
+            "sm_mhz": statistics.median(s for s, _, _ in self.samples),
+            "sm_max_mhz": self.max_mhz,
             "reasons": reasons,
-            "samples": len(rows),
+            "power_w_max": round(max(p for _, p, _ in self.samples), 1),
+            "samples": len(self.samples),
+            "source": "NVML polled every ~1 ms during the timed region",
         }
 
 
@@ -263,7 +319,7 @@ def run_cuda(args: argparse.Namespace, world: int, rank: int, local: int) -> Non
                                 device_id=dev)  # fmt: skip
     ops.load_library()
 
-    case = decode_workload(seed=rank, batch=args.batch)
+    case = decode_workload(seed=rank, batch=args.batch, num_blocks=args.pool_blocks)
     B, hq, hkv, d, bs = case.batch, case.num_q_heads, case.num_kv_heads, case.head_dim, 16
     dt = torch.bfloat16
     g = torch.Generator(device=dev).manual_seed(1000 + rank)
@@ -303,7 +359,7 @@ def run_cuda(args: argparse.Namespace, world: int, rank: int, local: int) -> Non
         step()
     barrier()
     ev = [torch.cuda.Event(enable_timing=True) for _ in range(2 * args.steps + 2)]
-    with ClockSampler(local) as clocks:
+    with ClockSampler(dev) as clocks:
         ev[0].record(stream)
         for i in range(args.steps):
             ops.reshape_and_cache(knew, vnew, kpool, vpool, slots)
@@ -317,6 +373,11 @@ def run_cuda(args: argparse.Namespace, world: int, rank: int, local: int) -> Non
     dec_ms = [ev[2 + 2 * i].elapsed_time(ev[3 + 2 * i]) for i in range(args.steps)]
     dec_avg = sum(dec_ms) / len(dec_ms) / 1e3
 
+    if args.skip_e2e:
+        if rank == 0:
+            print(json.dumps({"profiling_run": True, "decode_avg_us": dec_avg * 1e6,
+                              "decode_bytes": decode_bytes}))  # fmt: skip
+        return
     # ---- end to end through the C-ABI with host buffers
     pin = lambda t: t.cpu().pin_memory()  # noqa: E731
     h_q, h_k, h_v = pin(q), pin(knew), pin(vnew)
@@ -394,10 +455,7 @@ def run_cuda(args: argparse.Namespace, world: int, rank: int, local: int) -> Non
             "gpu_launches": 3 * args.steps,
             "clocks": clocks.summary(),
         }
-        traffic = ROOT / "profiles" / "decode_traffic.json"
-        if traffic.exists():
-            tr = json.loads(traffic.read_text())
-            line["roofline"]["traffic"] = tr.get("bytes_per_full_launch")
+        line["roofline"]["traffic"] = measured_traffic(decode_bytes)
         if world == 1 and not args.no_cpu_baseline:
             seqs, ks, vs, qs = gather_sample(case, kpool, vpool, q, 96 * 2**20)
             threads = os.cpu_count() or 1

@@ -147,7 +147,7 @@ async def drive(engine: Engine, clock: VirtualClock, arrivals: list[float],
 
 
 def make_sim_trace() -> None:
-    bs, nb = 4, 40
+    bs, nb = 4, 20
     tok = ByteTokenizer()
     backend = SimulatedBackend(SimulatedBackendConfig(0, 0, verify_kv=True), block_size=bs,
                                num_blocks=nb, eos_token_id=tok.eos_token_id)  # fmt: skip
