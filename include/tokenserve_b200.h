@@ -110,6 +110,36 @@ int ts_paged_decode(void* out, const void* query, int64_t query_token_stride,
                     int32_t block_size, int64_t num_blocks, float scale, int32_t dtype,
                     void* workspace, size_t workspace_bytes, void* stream);
 
+/* Size of the device scratch built into the library for ts_paged_decode_no_alloc (32 MiB). */
+#define TS_NO_ALLOC_SCRATCH_BYTES (32u << 20)
+
+/*
+ * K2 without a workspace argument. No counterpart in the reference: tokenserve has no native
+ * code at all; this entry point exists only for callers of this library that cannot allocate.
+ *
+ * Some callers cannot hand ts_paged_decode a workspace: a C or FFI caller embedded in a
+ * process whose device memory is owned by another allocator (a framework's caching allocator
+ * that has reserved the HBM, so a cudaMalloc next to it fails or fragments it), or a caller on
+ * a latency-critical path that must not call cudaMalloc/cudaFree, which can synchronise the
+ * device. This variant takes the same arguments minus the workspace and allocates nothing:
+ * its scratch is a TS_NO_ALLOC_SCRATCH_BYTES array inside the library's device image, which
+ * every GPU that loads the library holds until the process exits.
+ *
+ *   - Sizes whose scratch (ts_paged_decode_workspace_size) exceeds TS_NO_ALLOC_SCRATCH_BYTES
+ *     are rejected with TS_ERR_WORKSPACE_TOO_SMALL before anything is launched.
+ *   - The first call on each device looks up the scratch's device address with that device
+ *     current; make that first call before any stream capture.
+ *   - All calls on a device share the one scratch array and each call clears the parts that
+ *     must start at zero. Calls whose kernels overlap on the GPU (different streams without
+ *     ordering between them) race on it and give wrong results: order them.
+ */
+int ts_paged_decode_no_alloc(void* out, const void* query, int64_t query_token_stride,
+                             const void* key_pool, const void* value_pool,
+                             const int32_t* block_tables, int32_t max_blocks_per_seq,
+                             const int32_t* context_lens, int32_t batch, int32_t num_q_heads,
+                             int32_t num_kv_heads, int32_t head_dim, int32_t block_size,
+                             int64_t num_blocks, float scale, int32_t dtype, void* stream);
+
 /*
  * K3 — paged chunked-prefill attention (causal): each sequence's new chunk of queries
  * attends to its cached prefix blocks plus the chunk itself, all read through the block

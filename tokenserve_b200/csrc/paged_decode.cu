@@ -651,3 +651,127 @@ extern "C" int ts_paged_decode(void* out, const void* query, int64_t query_token
   TS_FAST(__half)
 #undef TS_FAST
 }
+
+// --------------------------------------------------------------------------- no-alloc variant
+//
+// ts_paged_decode_no_alloc runs the same decode kernels as ts_paged_decode, but its scratch
+// (partition partials, prefix sums, counters) lives in the file-scope device array below
+// instead of a caller-provided workspace. It exists for callers that cannot allocate device
+// memory for a workspace. The array is part of this library's device image, so every GPU
+// that loads the library holds kStaticScratchBytes until the process exits.
+
+namespace {
+
+constexpr size_t kStaticScratchBytes = size_t(TS_NO_ALLOC_SCRATCH_BYTES);
+static __device__ __align__(256) uint8_t g_decode_scratch[kStaticScratchBytes];
+
+constexpr int kMaxDevices = 64;
+std::mutex g_scratch_mu;
+void* g_scratch_ptr[kMaxDevices] = {};
+
+// Device address of g_decode_scratch on the current device. In host code the array's name is
+// only a host-side stand-in, so the real address is looked up once per device (with that
+// device current) and cached.
+int static_scratch(void** ptr) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess)
+    return ts::set_error(static_cast<int>(e), "paged_decode_no_alloc: cudaGetDevice: %s",
+                         cudaGetErrorString(e));
+  if (dev < 0 || dev >= kMaxDevices)
+    return ts::set_error(TS_ERR_UNSUPPORTED, "paged_decode_no_alloc: device %d", dev);
+  std::lock_guard<std::mutex> lock(g_scratch_mu);
+  if (g_scratch_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_decode_scratch);
+    if (e != cudaSuccess || p == nullptr)
+      return ts::set_error(static_cast<int>(e == cudaSuccess ? cudaErrorInvalidSymbol : e),
+                           "paged_decode_no_alloc: cudaGetSymbolAddress: %s",
+                           cudaGetErrorString(e));
+    g_scratch_ptr[dev] = p;
+  }
+  *ptr = g_scratch_ptr[dev];
+  return TS_OK;
+}
+
+}  // namespace
+
+extern "C" int ts_paged_decode_no_alloc(void* out, const void* query, int64_t query_token_stride,
+                                        const void* key_pool, const void* value_pool,
+                                        const int32_t* block_tables, int32_t max_blocks_per_seq,
+                                        const int32_t* context_lens, int32_t batch,
+                                        int32_t num_q_heads, int32_t num_kv_heads,
+                                        int32_t head_dim, int32_t block_size, int64_t num_blocks,
+                                        float scale, int32_t dtype, void* stream) {
+  if (ts::dtype_size(dtype) == 0)
+    return ts::set_error(TS_ERR_INVALID_ARGUMENT, "paged_decode_no_alloc: bad dtype %d", dtype);
+  if (batch < 0 || num_q_heads <= 0 || num_kv_heads <= 0 || num_q_heads % num_kv_heads ||
+      head_dim <= 0 || block_size <= 0 || num_blocks <= 0 || max_blocks_per_seq <= 0)
+    return ts::set_error(TS_ERR_INVALID_ARGUMENT,
+                         "paged_decode_no_alloc: bad sizes (batch %d, heads %d/%d, head_dim %d, "
+                         "block_size %d, blocks %lld, max_blocks %d)",
+                         batch, num_q_heads, num_kv_heads, head_dim, block_size,
+                         (long long)num_blocks, max_blocks_per_seq);
+  if (query_token_stride < int64_t(num_q_heads) * head_dim)
+    return ts::set_error(TS_ERR_INVALID_ARGUMENT, "paged_decode_no_alloc: query stride too small");
+  if (batch == 0) return ts::ok();
+  if (!out || !query || !key_pool || !value_pool || !block_tables || !context_lens)
+    return ts::set_error(TS_ERR_INVALID_ARGUMENT, "paged_decode_no_alloc: null pointer");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (!fast_path(num_q_heads, num_kv_heads, head_dim, block_size, dtype, num_blocks, key_pool,
+                 value_pool, query, query_token_stride, out))
+    return ts::paged_attention_portable(out, query, query_token_stride, key_pool, value_pool,
+                                        block_tables, max_blocks_per_seq, nullptr, context_lens,
+                                        batch, batch, num_q_heads, num_kv_heads, head_dim,
+                                        block_size, num_blocks, scale, dtype, s);
+  if (batch > 8192)
+    return ts::set_error(TS_ERR_UNSUPPORTED, "paged_decode_no_alloc: batch %d above 8192", batch);
+  const int group = num_q_heads / num_kv_heads;
+  const int nt = group > 8 ? 2 : 1;
+  const WsLayout w = ws_layout(batch, num_kv_heads, head_dim, max_blocks_per_seq, nt);
+  if (w.total > kStaticScratchBytes)
+    return ts::set_error(TS_ERR_WORKSPACE_TOO_SMALL,
+                         "paged_decode_no_alloc: these sizes need %zu bytes of scratch but the "
+                         "built-in scratch holds %zu; lower batch or max_blocks_per_seq, or call "
+                         "ts_paged_decode with a workspace",
+                         w.total, kStaticScratchBytes);
+  void* scratch = nullptr;
+  if (const int rc = static_scratch(&scratch); rc != TS_OK) return rc;
+  CUtensorMap km, vm;
+  const int64_t rows = num_blocks * num_kv_heads * kBlock;
+  if (!make_pool_map(&km, key_pool, rows, head_dim, dtype) ||
+      !make_pool_map(&vm, value_pool, rows, head_dim, dtype))
+    return ts::set_error(TS_ERR_INVALID_ARGUMENT,
+                         "paged_decode_no_alloc: cannot encode TMA map of pool");
+  // The prep kernel zeroes the work counter, status word and arrival counters at the start of
+  // every call; the partial-result slots are always written before they are read.
+  uint8_t* ws = static_cast<uint8_t*>(scratch);
+  DecodeArgs a;
+  a.out = out;
+  a.query = query;
+  a.q_stride = query_token_stride;
+  a.block_tables = block_tables;
+  a.context_lens = context_lens;
+  a.max_blocks = max_blocks_per_seq;
+  a.batch = batch;
+  a.num_q_heads = num_q_heads;
+  a.num_kv_heads = num_kv_heads;
+  a.group = group;
+  a.num_blocks = num_blocks;
+  a.scale_log2 = scale * kLog2e;
+  a.header = reinterpret_cast<int*>(ws);
+  a.prefix = reinterpret_cast<int*>(ws + w.prefix);
+  a.arrive = reinterpret_cast<int*>(ws + w.arrive);
+  a.part_o = reinterpret_cast<float*>(ws + w.part_o);
+  a.part_ml = reinterpret_cast<float2*>(ws + w.part_ml);
+#define TS_FAST_NA(T)                                                          \
+  if (head_dim == 128)                                                         \
+    return nt == 1 ? launch_fast<T, 128, 1>(a, km, vm, s)                      \
+                   : launch_fast<T, 128, 2>(a, km, vm, s);                     \
+  return nt == 1 ? launch_fast<T, 64, 1>(a, km, vm, s) : launch_fast<T, 64, 2>(a, km, vm, s);
+  if (dtype == TS_BFLOAT16) {
+    TS_FAST_NA(__nv_bfloat16)
+  }
+  TS_FAST_NA(__half)
+#undef TS_FAST_NA
+}
