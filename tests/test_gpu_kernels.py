@@ -208,17 +208,26 @@ def test_paged_decode_rejects_small_workspace(cuda_device) -> None:  # type: ign
 # ------------------------------------------------------------------------------ K3
 
 
+PREFILL_SHAPES = [(0, 37), (16, 20), (37, 64), (128, 2), (5, 129), (300, 200), (1000, 300)]
+
+
 @pytest.mark.parametrize(
     ("dtype", "hq", "hkv", "head_dim"),
     [
-        (torch.bfloat16, 32, 8, 128),
-        (torch.float16, 8, 2, 64),
-        (torch.float32, 4, 2, 64),
+        (torch.bfloat16, 32, 8, 128),  # tcgen05 path, G=4 (Llama-3-8B)
+        (torch.bfloat16, 64, 8, 128),  # tcgen05, G=8 (Llama-3-70B)
+        (torch.float16, 16, 1, 128),  # tcgen05, G=16
+        (torch.bfloat16, 4, 2, 128),  # tcgen05, G=2
+        (torch.float16, 2, 2, 128),  # tcgen05, G=1
+        (torch.bfloat16, 12, 4, 128),  # G=3: CUDA-core path
+        (torch.float16, 8, 2, 64),  # head_dim 64: CUDA-core path
+        (torch.float32, 4, 2, 64),  # tiny Llama, CUDA-core path
     ],
 )
 def test_paged_prefill_matches_oracle(cuda_device, dtype, hq, hkv, head_dim) -> None:  # type: ignore[no-untyped-def]
-    # (cached prefix, chunk): chunks start on and off block boundaries; one pure prompt.
-    shapes = [(0, 37), (16, 20), (37, 64), (128, 2), (5, 129), (300, 200)]
+    # (cached prefix, chunk): chunks start on and off block boundaries; one pure prompt; one
+    # long prefix spanning many 128-token KV tiles and a chunk spanning many query tiles.
+    shapes = PREFILL_SHAPES
     ctx = [p + c for p, c in shapes]
     case = small_paged_case(21, ctx, num_q_heads=hq, num_kv_heads=hkv, head_dim=head_dim)
     k, v, dk, dv = make_pools(case, dtype, cuda_device)
@@ -231,11 +240,32 @@ def test_paged_prefill_matches_oracle(cuda_device, dtype, hq, hkv, head_dim) -> 
         q.float().numpy(), k.float().numpy(), v.float().numpy(), case.block_tables, qsl,
         case.context_lens, scale,
     )  # fmt: skip
-    out = torch.empty_like(q, device=cuda_device)
-    ops.paged_prefill(
-        out, q.to(cuda_device), dk, dv, torch.from_numpy(case.block_tables).to(cuda_device),
-        torch.from_numpy(qsl).to(cuda_device), torch.from_numpy(case.context_lens).to(cuda_device),
-        max(c for _, c in shapes), scale,
-    )  # fmt: skip
+    out = torch.full(q.shape, 5.0, dtype=dtype, device=cuda_device)
+    for _ in range(2):
+        ops.paged_prefill(
+            out, q.to(cuda_device), dk, dv, torch.from_numpy(case.block_tables).to(cuda_device),
+            torch.from_numpy(qsl).to(cuda_device),
+            torch.from_numpy(case.context_lens).to(cuda_device), max(c for _, c in shapes), scale,
+        )  # fmt: skip
+        torch.cuda.synchronize()
+        assert_attention_close(out, ref, dtype)
+
+
+def test_paged_prefill_strided_query(cuda_device) -> None:  # type: ignore[no-untyped-def]
+    """Q as a slice of a fused QKV projection (token stride > Hq * D), as the model passes it."""
+    dtype, hq, hkv, d = torch.bfloat16, 32, 8, 128
+    shapes = [(40, 70), (0, 33)]
+    case = small_paged_case(6, [p + c for p, c in shapes], num_q_heads=hq, num_kv_heads=hkv)
+    k, v, dk, dv = make_pools(case, dtype, cuda_device)
+    qsl = np.array([0, 70, 103], dtype=np.int32)
+    fused = (torch.randn(103, hq + 2 * hkv, d) * 0.5).to(dtype)
+    q = fused[:, :hq]
+    ref = oatt.paged_prefill_np(q.float().numpy(), k.float().numpy(), v.float().numpy(),
+                                case.block_tables, qsl, case.context_lens, d**-0.5)  # fmt: skip
+    out = torch.empty(103, hq, d, dtype=dtype, device=cuda_device)
+    ops.paged_prefill(out, fused.to(cuda_device)[:, :hq], dk, dv,
+                      torch.from_numpy(case.block_tables).to(cuda_device),
+                      torch.from_numpy(qsl).to(cuda_device),
+                      torch.from_numpy(case.context_lens).to(cuda_device), 70, d**-0.5)  # fmt: skip
     torch.cuda.synchronize()
     assert_attention_close(out, ref, dtype)

@@ -5,7 +5,26 @@
 // (src/tokenserve/backends/hf.py:71), except that the prefix comes from cached blocks of the
 // paged pool (src/tokenserve/kv_cache.py:159-177) instead of being recomputed. Query row j of a
 // sequence whose step ends at context_lens[s] sits at position context_lens[s] - q_len + j.
+//
+// bf16/fp16, head_dim 128, block 16, G = Hq/Hkv in {1,2,4,8,16}: tcgen05 tensor-core kernel.
+//   * CTA = (sequence, KV head, query tile). The tile's 128 rows are 128/G query tokens x the
+//     G query heads of the KV head (GQA packing), so each K/V tile feeds all G heads.
+//   * warp 4 (producer): Q tile by one 3-D TMA box per 64-column half, then K/V tiles of 128
+//     tokens (8 blocks, gathered through the block table with 2-D TMA boxes, 128-byte swizzle,
+//     no multicast) into a 2-stage ring.
+//   * warp 5 (one lane): tcgen05.mma S = Q K^T (M=N=K=128, both K-major) into one of two TMEM
+//     S buffers, then O += P V with P read from TMEM (bf16, written over S) and V MN-major.
+//     QK of tile j+1 is issued before PV of tile j so it overlaps the softmax of tile j.
+//   * warps 0-3 (128 threads, thread = row = TMEM lane): online softmax in fp32 (exp2 domain)
+//     with the causal mask, P back to TMEM, O rescale in TMEM, and the epilogue.
+// Other shapes and fp32 use the CUDA-core kernel in attention_portable.cu.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
 #include "common.cuh"
+#include "tcgen05.cuh"
 
 namespace ts {
 int paged_attention_portable(void* out, const void* query, int64_t q_stride, const void* kp,
@@ -14,6 +33,361 @@ int paged_attention_portable(void* out, const void* query, int64_t q_stride, con
                              int hq, int hkv, int hd, int bs, int64_t nb, float scale, int dtype,
                              cudaStream_t s);
 }
+
+namespace {
+
+constexpr int kRows = 128;                   // query rows per tile (M)
+constexpr int kKvTile = 128;                 // KV tokens per tile (N of QK, K of PV)
+constexpr int kBlock = 16;                   // tokens per KV block
+constexpr int kHalfBytes = 128 * 128;        // 128 rows x 128 bytes (64 columns)
+constexpr int kTileBytes = 2 * kHalfBytes;   // 128 x 128 16-bit elements
+constexpr int kSmemBytes = 5 * kTileBytes + 256 + 1024;
+constexpr int kThreads = 192;
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr uint32_t kTmemCols = 512;  // S0 [0,128), S1 [128,256), O [256,384)
+
+struct PrefillArgs {
+  void* out;
+  const int32_t* block_tables;
+  const int32_t* qsl;
+  const int32_t* context_lens;
+  int max_blocks;
+  int num_q_heads;
+  int num_kv_heads;
+  int group;
+  int tq;  // query tokens per tile = 128 / group
+  float scale_log2;
+};
+
+struct Bars {
+  uint64_t q_full, k_full[2], v_full[2], kv_empty[2], s_full[2], p_full[2], pv_done;
+  uint32_t tmem;
+  int abort;
+};
+
+// Bounded wait that also gives up as soon as another role has aborted.
+__device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t phase, volatile int* abort) {
+  for (long long i = 0; i < ts::kMaxSpins; ++i) {
+    if (ts::mbar_try_wait(bar, phase)) return true;
+    if ((i & 255) == 255 && *abort) return false;
+  }
+  *abort = 1;
+  return false;
+}
+
+template <bool BF16>
+__global__ void __launch_bounds__(kThreads, 1)
+    paged_prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap,
+                            const __grid_constant__ CUtensorMap kmap,
+                            const __grid_constant__ CUtensorMap vmap, const PrefillArgs a) {
+  using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
+  using Mma = ts::MmaOp<T>;
+  const int tile = blockIdx.x, h = blockIdx.y, seq = blockIdx.z;
+  const int q0 = a.qsl[seq];
+  const int q_len = a.qsl[seq + 1] - q0;
+  if (tile * a.tq >= q_len) return;
+  int ctx = a.context_lens[seq];
+  if (ctx > a.max_blocks * kBlock) ctx = a.max_blocks * kBlock;
+  const int p0 = ctx - q_len;
+  if (p0 < 0) return;
+  const int last_q = min(q_len, (tile + 1) * a.tq) - 1;
+  const int n_kv = p0 + last_q + 1;  // keys this tile can see
+  const int n_tiles = (n_kv + kKvTile - 1) / kKvTile;
+  const int total_blk = (n_kv + kBlock - 1) / kBlock;
+
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = ts::smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + (((raw + 1023) & ~1023u) - raw);
+  uint8_t* sQ = smem;
+  auto sK = [&](int st) { return smem + kTileBytes + st * 2 * kTileBytes; };
+  auto sV = [&](int st) { return smem + 2 * kTileBytes + st * 2 * kTileBytes; };
+  Bars* bars = reinterpret_cast<Bars*>(smem + 5 * kTileBytes);
+  volatile int* abort = &bars->abort;
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  if (threadIdx.x == 0) {
+    ts::mbar_init(&bars->q_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      ts::mbar_init(&bars->k_full[i], 1);
+      ts::mbar_init(&bars->v_full[i], 1);
+      ts::mbar_init(&bars->kv_empty[i], 1);
+      ts::mbar_init(&bars->s_full[i], 1);
+      ts::mbar_init(&bars->p_full[i], 128);
+    }
+    ts::mbar_init(&bars->pv_done, 1);
+    bars->abort = 0;
+    ts::fence_mbar_init();
+  }
+  if (warp == 0) {
+    ts::tc::tmem_alloc(&bars->tmem, kTmemCols);
+    ts::tc::tmem_relinquish();
+  }
+  ts::tc::fence_before_sync();
+  __syncthreads();
+  ts::tc::fence_after_sync();
+  const uint32_t tmem = bars->tmem;
+  const int G = a.group;
+
+  if (warp == 4) {
+    // ------------------------------------------------------------ producer (TMA)
+    const int32_t* table = a.block_tables + int64_t(seq) * a.max_blocks;
+    if (lane == 0) {
+      ts::mbar_arrive_expect_tx(&bars->q_full, kTileBytes);
+      ts::tc::tma_load_3d(sQ, &qmap, &bars->q_full, 0, h * G, q0 + tile * a.tq);
+      ts::tc::tma_load_3d(sQ + kHalfBytes, &qmap, &bars->q_full, 64, h * G, q0 + tile * a.tq);
+    }
+    int issued = 0;
+    for (int j = 0; j < n_tiles; ++j) {
+      const int st = j & 1;
+      if (j >= 2 && !wait_bar(&bars->kv_empty[st], ((j - 2) >> 1) & 1, abort)) break;
+      const int blk0 = j * (kKvTile / kBlock);
+      const int nb = min(kKvTile / kBlock, total_blk - blk0);
+      const int phys_l = lane < nb ? __ldg(table + blk0 + lane) : 0;
+      if (lane == 0) {
+        ts::mbar_arrive_expect_tx(&bars->k_full[st], nb * 2 * 2048);
+        ts::mbar_arrive_expect_tx(&bars->v_full[st], nb * 2 * 2048);
+      }
+      for (int b = 0; b < kKvTile / kBlock; ++b) {
+        const int phys = __shfl_sync(0xffffffffu, phys_l, b);
+        if (lane == 0 && b < nb) {
+          const int row = (phys * a.num_kv_heads + h) * kBlock;
+          for (int hf = 0; hf < 2; ++hf) {
+            ts::tma_load_2d(sK(st) + hf * kHalfBytes + b * 2048, &kmap, &bars->k_full[st],
+                            hf * 64, row);
+            ts::tma_load_2d(sV(st) + hf * kHalfBytes + b * 2048, &vmap, &bars->v_full[st],
+                            hf * 64, row);
+          }
+        }
+      }
+      issued = j + 1;
+    }
+    if (*abort && lane == 0) {
+      // Let the copies still in flight land before shared memory is released.
+      for (int j = max(0, issued - 2); j < issued; ++j) {
+        ts::mbar_wait_bounded(&bars->k_full[j & 1], (j >> 1) & 1);
+        ts::mbar_wait_bounded(&bars->v_full[j & 1], (j >> 1) & 1);
+      }
+      ts::mbar_wait_bounded(&bars->q_full, 0);
+    }
+  } else if (warp == 5) {
+    // ------------------------------------------------------------ MMA issuer (one lane)
+    if (lane == 0) {
+      constexpr uint32_t idesc_qk = ts::tc::idesc_f16(BF16, kRows, kKvTile, false);
+      constexpr uint32_t idesc_pv = ts::tc::idesc_f16(BF16, kRows, 128, true);
+      const uint32_t q_addr = ts::smem_u32(sQ);
+      int last_pv = -1;
+      auto issue_qk = [&](int j) -> bool {
+        const int st = j & 1;
+        if (!wait_bar(&bars->k_full[st], (j >> 1) & 1, abort)) return false;
+        ts::tc::fence_after_sync();
+        const uint32_t k_addr = ts::smem_u32(sK(st));
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          const uint32_t off = (kk >> 2) * kHalfBytes + (kk & 3) * 32;
+          ts::tc::mma_ss(tmem + st * 128, ts::tc::smem_desc_sw128(q_addr + off, 16, 1024),
+                         ts::tc::smem_desc_sw128(k_addr + off, 16, 1024), idesc_qk, kk > 0);
+        }
+        ts::tc::commit(&bars->s_full[st]);
+        return true;
+      };
+      bool ok = wait_bar(&bars->q_full, 0, abort) && issue_qk(0);
+      for (int j = 0; ok && j < n_tiles; ++j) {
+        if (j + 1 < n_tiles && !issue_qk(j + 1)) break;
+        const int st = j & 1;
+        if (!wait_bar(&bars->p_full[st], (j >> 1) & 1, abort) ||
+            !wait_bar(&bars->v_full[st], (j >> 1) & 1, abort))
+          break;
+        ts::tc::fence_after_sync();
+        const uint32_t v_addr = ts::smem_u32(sV(st));
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk)
+          ts::tc::mma_ts(tmem + 256, tmem + st * 128 + kk * 8,
+                         ts::tc::smem_desc_sw128(v_addr + kk * 2048, kHalfBytes, 1024), idesc_pv,
+                         j > 0 || kk > 0);
+        ts::tc::commit(&bars->pv_done);
+        if (j + 2 < n_tiles) ts::tc::commit(&bars->kv_empty[st]);
+        last_pv = j;
+      }
+      if (*abort && last_pv >= 0) ts::mbar_wait_bounded(&bars->pv_done, last_pv & 1);
+    }
+  } else {
+    // ------------------------------------------------------------ softmax / epilogue
+    const int r = threadIdx.x;  // tile row == TMEM lane
+    const int i = r / G, g = r - (r / G) * G;
+    const int qi = tile * a.tq + i;
+    const bool row_valid = qi < q_len;
+    const int pos = p0 + (row_valid ? qi : q_len - 1);
+    const uint32_t lane_base = tmem + (uint32_t(warp * 32) << 16);
+    float m_run = -INFINITY, l_run = 0.f;
+    bool ok = true;
+    for (int j = 0; j < n_tiles; ++j) {
+      const int st = j & 1;
+      if (!wait_bar(&bars->s_full[st], (j >> 1) & 1, abort)) {
+        ok = false;
+        break;
+      }
+      ts::tc::fence_after_sync();
+      float s[128];
+#pragma unroll
+      for (int c4 = 0; c4 < 4; ++c4) {
+        uint32_t rr[32];
+        ts::tc::tmem_ld32(lane_base + st * 128 + c4 * 32, rr);
+        ts::tc::wait_ld();
+#pragma unroll
+        for (int c = 0; c < 32; ++c) s[c4 * 32 + c] = __uint_as_float(rr[c]);
+      }
+      const int limit = pos - j * kKvTile;  // columns c <= limit are visible
+      float mx = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < 128; ++c) {
+        s[c] = c <= limit ? s[c] * a.scale_log2 : -INFINITY;
+        mx = fmaxf(mx, s[c]);
+      }
+      const float m_new = fmaxf(m_run, mx);
+      const float corr = exp2f(m_run - m_new);
+      float sum = 0.f;
+#pragma unroll
+      for (int c = 0; c < 128; ++c) {
+        s[c] = exp2f(s[c] - m_new);
+        sum += s[c];
+      }
+      l_run = l_run * corr + sum;
+      m_run = m_new;
+      if (j > 0) {
+        if (!wait_bar(&bars->pv_done, (j - 1) & 1, abort)) {
+          ok = false;
+          break;
+        }
+        ts::tc::fence_after_sync();
+        if (__any_sync(0xffffffffu, corr != 1.f)) {
+#pragma unroll
+          for (int c4 = 0; c4 < 4; ++c4) {
+            uint32_t rr[32];
+            ts::tc::tmem_ld32(lane_base + 256 + c4 * 32, rr);
+            ts::tc::wait_ld();
+#pragma unroll
+            for (int c = 0; c < 32; ++c) rr[c] = __float_as_uint(__uint_as_float(rr[c]) * corr);
+            ts::tc::tmem_st32(lane_base + 256 + c4 * 32, rr);
+          }
+        }
+      }
+#pragma unroll
+      for (int hf = 0; hf < 2; ++hf) {
+        uint32_t pk[32];
+#pragma unroll
+        for (int c = 0; c < 32; ++c) pk[c] = Mma::pack(s[64 * hf + 2 * c], s[64 * hf + 2 * c + 1]);
+        ts::tc::tmem_st32(lane_base + st * 128 + 32 * hf, pk);
+      }
+      ts::tc::wait_st();
+      if (j * kKvTile + kKvTile > n_kv) {
+        // Rows past the last visible key hold stale or unwritten data: zero them so that
+        // P = 0 times V stays 0.
+        if (!wait_bar(&bars->v_full[st], (j >> 1) & 1, abort)) {
+          ok = false;
+          break;
+        }
+        if (j * kKvTile + r >= n_kv) {
+          uint4* v0 = reinterpret_cast<uint4*>(sV(st) + r * 128);
+          uint4* v1 = reinterpret_cast<uint4*>(sV(st) + kHalfBytes + r * 128);
+#pragma unroll
+          for (int c = 0; c < 8; ++c) v0[c] = v1[c] = make_uint4(0, 0, 0, 0);
+        }
+        ts::fence_proxy_async_smem();
+      }
+      ts::tc::fence_before_sync();
+      ts::mbar_arrive(&bars->p_full[st]);
+    }
+    if (ok && wait_bar(&bars->pv_done, (n_tiles - 1) & 1, abort)) {
+      ts::tc::fence_after_sync();
+      const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
+      T* orow = static_cast<T*>(a.out) +
+                (int64_t(q0 + qi) * a.num_q_heads + h * G + g) * 128;
+#pragma unroll
+      for (int c4 = 0; c4 < 4; ++c4) {
+        uint32_t rr[32];
+        ts::tc::tmem_ld32(lane_base + 256 + c4 * 32, rr);
+        ts::tc::wait_ld();
+        uint32_t pk[16];
+#pragma unroll
+        for (int c = 0; c < 16; ++c)
+          pk[c] = Mma::pack(__uint_as_float(rr[2 * c]) * inv, __uint_as_float(rr[2 * c + 1]) * inv);
+        if (row_valid) {
+          uint4* dst = reinterpret_cast<uint4*>(orow + c4 * 32);
+#pragma unroll
+          for (int c = 0; c < 4; ++c)
+            dst[c] = make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
+        }
+      }
+    }
+  }
+  ts::tc::fence_before_sync();
+  __syncthreads();
+  if (warp == 0) {
+    ts::tc::fence_after_sync();
+    ts::tc::tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+// --------------------------------------------------------------------------- host side
+
+PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+CUtensorMapDataType tma_type(int dtype) {
+  return dtype == TS_BFLOAT16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+}
+
+bool encode_pool_map(CUtensorMap* map, const void* pool, int64_t rows, int dtype) {
+  const cuuint64_t dims[2] = {128, cuuint64_t(rows)};
+  const cuuint64_t strides[1] = {256};
+  const cuuint32_t box[2] = {64, kBlock};
+  const cuuint32_t estr[2] = {1, 1};
+  return get_encode()(map, tma_type(dtype), 2, const_cast<void*>(pool), dims, strides, box, estr,
+                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                      CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// Query rows [tokens][heads][128] with a token stride; box = (64 columns, G heads, 128/G tokens).
+bool encode_query_map(CUtensorMap* map, const void* q, int64_t tokens, int hq, int64_t q_stride,
+                      int group, int dtype) {
+  const cuuint64_t dims[3] = {128, cuuint64_t(hq), cuuint64_t(tokens)};
+  const cuuint64_t strides[2] = {256, cuuint64_t(q_stride) * 2};
+  const cuuint32_t box[3] = {64, cuuint32_t(group), cuuint32_t(kRows / group)};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  return get_encode()(map, tma_type(dtype), 3, const_cast<void*>(q), dims, strides, box, estr,
+                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                      CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+bool tc_path(int hq, int hkv, int hd, int bs, int dtype, int64_t num_blocks, const void* kp,
+             const void* vp, const void* q, int64_t q_stride, const void* out, int num_seqs) {
+  if (dtype != TS_BFLOAT16 && dtype != TS_FLOAT16) return false;
+  if (hd != 128 || bs != kBlock || hkv <= 0 || hq % hkv) return false;
+  const int g = hq / hkv;
+  if (g != 1 && g != 2 && g != 4 && g != 8 && g != 16) return false;
+  if (num_blocks * hkv * kBlock >= (int64_t(1) << 31) || num_seqs > 65535 || hkv > 65535)
+    return false;
+  if ((reinterpret_cast<uint64_t>(kp) | reinterpret_cast<uint64_t>(vp) |
+       reinterpret_cast<uint64_t>(q) | reinterpret_cast<uint64_t>(out)) % 16)
+    return false;
+  if ((q_stride * 2) % 16) return false;
+  return get_encode() != nullptr;
+}
+
+}  // namespace
 
 extern "C" int ts_paged_prefill(void* out, const void* query, int64_t query_token_stride,
                                 const void* key_pool, const void* value_pool,
@@ -39,9 +413,43 @@ extern "C" int ts_paged_prefill(void* out, const void* query, int64_t query_toke
   if (!out || !query || !key_pool || !value_pool || !block_tables || !query_start_loc ||
       !context_lens)
     return ts::set_error(TS_ERR_INVALID_ARGUMENT, "paged_prefill: null pointer");
-  return ts::paged_attention_portable(out, query, query_token_stride, key_pool, value_pool,
-                                      block_tables, max_blocks_per_seq, query_start_loc,
-                                      context_lens, num_seqs, num_query_tokens, num_q_heads,
-                                      num_kv_heads, head_dim, block_size, num_blocks, scale,
-                                      dtype, static_cast<cudaStream_t>(stream));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (!tc_path(num_q_heads, num_kv_heads, head_dim, block_size, dtype, num_blocks, key_pool,
+               value_pool, query, query_token_stride, out, num_seqs))
+    return ts::paged_attention_portable(out, query, query_token_stride, key_pool, value_pool,
+                                        block_tables, max_blocks_per_seq, query_start_loc,
+                                        context_lens, num_seqs, num_query_tokens, num_q_heads,
+                                        num_kv_heads, head_dim, block_size, num_blocks, scale,
+                                        dtype, s);
+  const int group = num_q_heads / num_kv_heads;
+  CUtensorMap qm, km, vm;
+  const int64_t rows = num_blocks * num_kv_heads * kBlock;
+  if (!encode_query_map(&qm, query, num_query_tokens, num_q_heads, query_token_stride, group,
+                        dtype) ||
+      !encode_pool_map(&km, key_pool, rows, dtype) || !encode_pool_map(&vm, value_pool, rows, dtype))
+    return ts::set_error(TS_ERR_INVALID_ARGUMENT, "paged_prefill: cannot encode TMA maps");
+  PrefillArgs a;
+  a.out = out;
+  a.block_tables = block_tables;
+  a.qsl = query_start_loc;
+  a.context_lens = context_lens;
+  a.max_blocks = max_blocks_per_seq;
+  a.num_q_heads = num_q_heads;
+  a.num_kv_heads = num_kv_heads;
+  a.group = group;
+  a.tq = kRows / group;
+  a.scale_log2 = scale * kLog2e;
+  const int tiles = (max_query_len + a.tq - 1) / a.tq;
+  if (tiles == 0) return ts::ok();
+  dim3 grid(tiles, num_kv_heads, num_seqs);
+  if (dtype == TS_BFLOAT16) {
+    auto kern = paged_prefill_tc_kernel<true>;
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+    kern<<<grid, kThreads, kSmemBytes, s>>>(qm, km, vm, a);
+  } else {
+    auto kern = paged_prefill_tc_kernel<false>;
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+    kern<<<grid, kThreads, kSmemBytes, s>>>(qm, km, vm, a);
+  }
+  return ts::launch_status("paged_prefill");
 }
