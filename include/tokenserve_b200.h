@@ -99,9 +99,9 @@ size_t ts_paged_decode_workspace_size(int32_t batch, int32_t num_q_heads, int32_
  * context_lens: int32 [batch]; tokens 0..context_lens[b]-1 (the new token included) are
  *               attended. 0 writes zeros.
  * scale:        softmax scale (head_dim ** -0.5 for Llama).
- * workspace:    device scratch of at least ts_paged_decode_workspace_size(...) bytes. Its
- *               first 4096 bytes must be zero before the first call (they are left zero
- *               after every completed call).
+ * workspace:    device scratch of at least ts_paged_decode_workspace_size(...) bytes, 256-byte
+ *               aligned, with no initial contents required (every call resets the counters it
+ *               uses). Calls that overlap on the GPU must not share a workspace.
  */
 int ts_paged_decode(void* out, const void* query, int64_t query_token_stride,
                     const void* key_pool, const void* value_pool, const int32_t* block_tables,

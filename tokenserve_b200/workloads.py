@@ -5,6 +5,10 @@
   256 sequences with log-normal context lengths (median 1024, sigma 1.0, clipped to 16..8192),
   block tables drawn without replacement from a seeded permutation of the pool, and Q/K/V
   ~ N(0, 1) * 0.5. Each step appends one K/V token per sequence, then attends.
+* :func:`prefill_workload` — chunked prefill with prefix caching at Llama-3-8B geometry: 64
+  sequences share one seeded 1024-token prefix already resident as cached blocks, each has a
+  unique suffix of uniform 256..2048 tokens, processed in 512-token chunks that attend causally
+  over the cached prefix plus the chunk itself.
 * :func:`small_paged_case` — the same construction at sizes a CPU oracle checks in seconds.
 
 Only numpy is used for the index arithmetic, so the same seed gives the same tables on every
@@ -93,3 +97,76 @@ def small_paged_case(
     nb = need + spare_blocks
     tables = tables_from_permutation(rng, ctx, nb, block_size)
     return PagedCase(nb, block_size, num_q_heads, num_kv_heads, head_dim, ctx, tables, seed)
+
+
+@dataclass
+class PrefillRound:
+    """One round of 512-token chunks: chunk k of every sequence that still has one."""
+
+    seqs: np.ndarray  # int64 [S] sequence ids
+    chunk_lens: np.ndarray  # int32 [S]
+    context_lens: np.ndarray  # int32 [S] cached prefix + chunk
+    query_start_loc: np.ndarray  # int32 [S + 1]
+    block_tables: np.ndarray  # int32 [S, W]
+    slot_mapping: np.ndarray  # int64 [sum(chunk_lens)]
+
+    @property
+    def num_tokens(self) -> int:
+        return int(self.query_start_loc[-1])
+
+    def flops(self, num_q_heads: int, head_dim: int) -> int:
+        """4 * Hq * D * sum over chunks of (c * n_prev + c (c + 1) / 2)."""
+        c = self.chunk_lens.astype(np.int64)
+        n_prev = self.context_lens.astype(np.int64) - c
+        return int(4 * num_q_heads * head_dim * (c * n_prev + c * (c + 1) // 2).sum())
+
+
+@dataclass
+class PrefillWorkload:
+    num_blocks: int
+    block_size: int
+    num_q_heads: int
+    num_kv_heads: int
+    head_dim: int
+    num_layers: int
+    suffix_lens: np.ndarray
+    rounds: list[PrefillRound]
+
+    def flops_per_layer(self) -> int:
+        return sum(r.flops(self.num_q_heads, self.head_dim) for r in self.rounds)
+
+
+def prefill_workload(seed: int = 0, num_seqs: int = 64, prefix: int = 1024, chunk: int = 512,
+                     num_layers: int = 32) -> PrefillWorkload:  # fmt: skip
+    """The chunked-prefill-with-prefix-cache workload (see module docstring)."""
+    rng = np.random.default_rng(seed)
+    bs = 16
+    suffix = rng.integers(256, 2049, num_seqs)
+    pre_blocks = prefix // bs
+    need = pre_blocks + int(((suffix + bs - 1) // bs).sum())
+    num_blocks = ((need + 1023) // 1024) * 1024
+    perm = rng.permutation(num_blocks).astype(np.int32)
+    shared = perm[:pre_blocks]
+    off = pre_blocks
+    tables = []
+    for L in suffix.tolist():
+        nb = (L + bs - 1) // bs
+        tables.append(np.concatenate([shared, perm[off : off + nb]]))
+        off += nb
+    rounds = []
+    for k in range((int(suffix.max()) + chunk - 1) // chunk):
+        seqs = np.nonzero(suffix > k * chunk)[0]
+        c = np.minimum(suffix[seqs] - k * chunk, chunk).astype(np.int32)
+        n_prev = prefix + k * chunk
+        ctx = (n_prev + c).astype(np.int32)
+        qsl = np.zeros(len(seqs) + 1, dtype=np.int32)
+        np.cumsum(c, out=qsl[1:])
+        width = max(len(tables[s]) for s in seqs)
+        bt = np.zeros((len(seqs), width), dtype=np.int32)
+        slots = []
+        for i, s in enumerate(seqs.tolist()):
+            bt[i, : len(tables[s])] = tables[s]
+            pos = np.arange(n_prev, n_prev + int(c[i]), dtype=np.int64)
+            slots.append(tables[s][pos // bs].astype(np.int64) * bs + pos % bs)
+        rounds.append(PrefillRound(seqs, c, ctx, qsl, bt, np.concatenate(slots)))
+    return PrefillWorkload(num_blocks, bs, 32, 8, 128, num_layers, suffix, rounds)
