@@ -26,9 +26,27 @@
 
 namespace {
 
-constexpr int kWarps = 8;
-constexpr int kBlock = 16;       // tokens per KV block (TMA box height)
-constexpr int kPartBlocks = 16;  // blocks per work item (256 tokens)
+// Tuning knobs (compile-time).
+#ifndef TS_DECODE_WARPS
+#define TS_DECODE_WARPS 8  // independent warp pipelines per CTA (one CTA per SM)
+#endif
+#ifndef TS_DECODE_PART_BLOCKS
+#define TS_DECODE_PART_BLOCKS 64  // blocks per work item
+#endif
+#ifndef TS_DECODE_STAGES_D128
+#define TS_DECODE_STAGES_D128 3  // ring stages per warp at head_dim 128
+#endif
+#ifndef TS_DECODE_ONE_BOX
+#define TS_DECODE_ONE_BOX 0  // 1: one 4 KiB TMA box per 128-dim tile instead of two 2 KiB
+#endif
+#ifndef TS_DECODE_LPT
+#define TS_DECODE_LPT 1  // 1: full partitions first, then partial ones by decreasing size
+#endif
+
+constexpr int kWarps = TS_DECODE_WARPS;
+constexpr int kBlock = 16;                          // tokens per KV block
+constexpr int kPartBlocks = TS_DECODE_PART_BLOCKS;  // blocks per work item
+static_assert(kPartBlocks >= 2 && kPartBlocks <= 64, "a work item's table fits two registers per lane");
 constexpr float kLog2e = 1.4426950408889634f;
 
 struct DecodeArgs {
@@ -44,8 +62,10 @@ struct DecodeArgs {
   int group;  // query heads per KV head
   int64_t num_blocks;
   float scale_log2;
-  int* header;  // [0] = work counter, [1] = status
+  int* header;  // [0] work counter, [1] status
   int* prefix;  // [batch + 1] partitions before sequence b
+  int4* part_info;  // [partition, in claim order] = (sequence, partition, slot partition, nparts)
+  int* part_ctx;     // [partition, in claim order] = context length of its sequence
   int* arrive;  // [batch * num_kv_heads]
   float* part_o;   // [slot][head_dim][NT * 8]
   float2* part_ml;  // [slot][NT * 8]
@@ -53,7 +73,7 @@ struct DecodeArgs {
 
 // Workspace layout (byte offsets), shared by the size query and the launcher.
 struct WsLayout {
-  size_t prefix, arrive, part_o, part_ml, total;
+  size_t prefix, part_info, part_ctx, arrive, part_o, part_ml, total;
 };
 
 inline size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
@@ -64,7 +84,9 @@ WsLayout ws_layout(int batch, int hkv, int hd, int max_blocks, int nt) {
       size_t(batch) * size_t((max_blocks + kPartBlocks - 1) / kPartBlocks);
   const size_t slots = max_parts * size_t(hkv);
   w.prefix = 256;
-  w.arrive = w.prefix + align256(sizeof(int) * (size_t(batch) + 1));
+  w.part_info = w.prefix + align256(sizeof(int) * (size_t(batch) + 1));
+  w.part_ctx = w.part_info + align256(sizeof(int4) * max_parts);
+  w.arrive = w.part_ctx + align256(sizeof(int) * max_parts);
   w.part_o = w.arrive + align256(sizeof(int) * size_t(batch) * hkv);
   w.part_ml = w.part_o + align256(sizeof(float) * slots * hd * nt * 8);
   w.total = w.part_ml + align256(sizeof(float2) * slots * nt * 8);
@@ -73,63 +95,112 @@ WsLayout ws_layout(int batch, int hkv, int hd, int max_blocks, int nt) {
 
 // --------------------------------------------------------------------------- prep kernel
 
-// One CTA: per-sequence partition counts -> exclusive prefix sums, zeroed counters, and zero
-// output rows for empty contexts.
-template <typename T>
-__global__ void __launch_bounds__(1024) decode_prep_kernel(DecodeArgs a, int row_elems) {
-  __shared__ int warp_sums[32];
-  const int B = a.batch;
-  const int per = (B + blockDim.x - 1) / blockDim.x;
-  const int b0 = threadIdx.x * per;
-  int local = 0;
-  for (int i = 0; i < per; ++i) {
-    const int b = b0 + i;
-    if (b < B) {
-      int ctx = a.context_lens[b];
-      ctx = ctx < 0 ? 0 : (ctx > a.max_blocks * kBlock ? a.max_blocks * kBlock : ctx);
-      local += (ctx + kPartBlocks * kBlock - 1) / (kPartBlocks * kBlock);
-    }
-  }
-  // Block-wide exclusive scan of `local`.
+// Block-wide exclusive scan (1 CTA); returns the exclusive prefix and sets *total.
+__device__ __forceinline__ int block_exclusive_scan(int v, int* total, int* warp_sums) {
   const int lane = threadIdx.x % 32, warp = threadIdx.x / 32;
-  int incl = local;
+  int incl = v;
 #pragma unroll
   for (int o = 1; o < 32; o <<= 1) {
-    const int v = __shfl_up_sync(0xffffffffu, incl, o);
-    if (lane >= o) incl += v;
+    const int x = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += x;
   }
+  __syncthreads();
   if (lane == 31) warp_sums[warp] = incl;
   __syncthreads();
   if (warp == 0) {
     int w = lane < (int)(blockDim.x / 32) ? warp_sums[lane] : 0;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
-      const int v = __shfl_up_sync(0xffffffffu, w, o);
-      if (lane >= o) w += v;
+      const int x = __shfl_up_sync(0xffffffffu, w, o);
+      if (lane >= o) w += x;
     }
     warp_sums[lane] = w;  // inclusive over warps
   }
   __syncthreads();
-  int run = incl - local + (warp > 0 ? warp_sums[warp - 1] : 0);
+  *total = warp_sums[blockDim.x / 32 - 1];
+  return incl - v + (warp > 0 ? warp_sums[warp - 1] : 0);
+}
+
+__device__ __forceinline__ int clamped_blocks(const DecodeArgs& a, int b) {
+  int ctx = a.context_lens[b];
+  ctx = ctx < 0 ? 0 : (ctx > a.max_blocks * kBlock ? a.max_blocks * kBlock : ctx);
+  return (ctx + kBlock - 1) / kBlock;
+}
+
+// One CTA: per-sequence partition counts -> prefix sums, and the descriptor of every work
+// partition in the order warps will claim them. With TS_DECODE_LPT the full partitions of all
+// sequences come first and the partial last partitions follow, longest first (counting sort),
+// so the kernel's tail is made of the shortest items. Also zeroes the counters and the output
+// rows of empty contexts.
+template <typename T>
+__global__ void __launch_bounds__(1024) decode_prep_kernel(DecodeArgs a, int row_elems) {
+  __shared__ int warp_sums[32];
+  __shared__ int hist[kPartBlocks], cursor[kPartBlocks];
+  const int B = a.batch;
+  const int per = (B + blockDim.x - 1) / blockDim.x;
+  const int b0 = threadIdx.x * per;
+  if (threadIdx.x < kPartBlocks) hist[threadIdx.x] = 0;
+  int parts = 0, full = 0;
   for (int i = 0; i < per; ++i) {
     const int b = b0 + i;
     if (b < B) {
-      a.prefix[b] = run;
-      int ctx = a.context_lens[b];
-      ctx = ctx < 0 ? 0 : (ctx > a.max_blocks * kBlock ? a.max_blocks * kBlock : ctx);
-      run += (ctx + kPartBlocks * kBlock - 1) / (kPartBlocks * kBlock);
-      if (ctx == 0) {
+      const int nblk = clamped_blocks(a, b);
+      parts += (nblk + kPartBlocks - 1) / kPartBlocks;
+      full += nblk / kPartBlocks;
+    }
+  }
+  __syncthreads();
+  int total_parts = 0, total_full = 0;
+  int run_p = block_exclusive_scan(parts, &total_parts, warp_sums);
+  int run_f = block_exclusive_scan(full, &total_full, warp_sums);
+  const int cap = a.max_blocks * kBlock;
+  for (int i = 0; i < per; ++i) {
+    const int b = b0 + i;
+    if (b < B) {
+      const int nblk = clamped_blocks(a, b);
+      const int ctx = min(max(a.context_lens[b], 0), cap);
+      const int np = (nblk + kPartBlocks - 1) / kPartBlocks, nf = nblk / kPartBlocks;
+      a.prefix[b] = run_p;
+      for (int p = 0; p < nf; ++p) {
+        const int idx = TS_DECODE_LPT ? run_f + p : run_p + p;
+        a.part_info[idx] = make_int4(b, p, run_p + p, np);
+        a.part_ctx[idx] = ctx;
+      }
+      if (nblk % kPartBlocks) atomicAdd(&hist[nblk % kPartBlocks], 1);
+      if (nblk == 0) {
         T* o = static_cast<T*>(a.out) + int64_t(b) * row_elems;
         for (int e = 0; e < row_elems; ++e) o[e] = ts::from_float<T>(0.f);
       }
+      run_p += np;
+      run_f += nf;
     }
   }
-  if (threadIdx.x == blockDim.x - 1) a.prefix[B] = run;
-  for (int i = threadIdx.x; i < B * a.num_kv_heads; i += blockDim.x) a.arrive[i] = 0;
+  __syncthreads();
   if (threadIdx.x == 0) {
+    a.prefix[B] = total_parts;
+    int off = total_full;
+    for (int sz = kPartBlocks - 1; sz >= 1; --sz) {  // longest partial partitions first
+      cursor[sz] = off;
+      off += hist[sz];
+    }
     a.header[0] = 0;
     a.header[1] = 0;
   }
+  __syncthreads();
+  for (int i = 0; i < per; ++i) {
+    const int b = b0 + i;
+    if (b < B) {
+      const int nblk = clamped_blocks(a, b);
+      const int r = nblk % kPartBlocks;
+      if (r) {
+        const int nf = nblk / kPartBlocks, pb = a.prefix[b];
+        const int idx = TS_DECODE_LPT ? atomicAdd(&cursor[r], 1) : pb + nf;
+        a.part_info[idx] = make_int4(b, nf, pb + nf, nf + 1);
+        a.part_ctx[idx] = min(max(a.context_lens[b], 0), cap);
+      }
+    }
+  }
+  for (int i = threadIdx.x; i < B * a.num_kv_heads; i += blockDim.x) a.arrive[i] = 0;
 }
 
 // --------------------------------------------------------------------------- main kernel
@@ -145,31 +216,43 @@ struct Geometry {
   static constexpr int kHalves = D / 64;              // 64-column TMA boxes per row
   static constexpr int kTileBytes = kBlock * D * 2;   // one block's K (or V) for one head
   static constexpr int kStageBytes = 2 * kTileBytes;  // K tile then V tile
-  static constexpr int kStages = D == 128 ? 3 : 6;
+  static constexpr int kStages = D == 128 ? TS_DECODE_STAGES_D128 : 6;
+  static constexpr bool kOneBox = TS_DECODE_ONE_BOX && D == 128;
   static constexpr int kRingBytes = kStages * kStageBytes;
-  static constexpr int kSmemBytes = kWarps * kRingBytes + kWarps * kStages * 16 + 1024;
+  // ring, then one mbarrier (8 B) and one item descriptor (32 B) per stage, + alignment slack
+  static constexpr int kBarBytes = (kWarps * kStages * 8 + 15) / 16 * 16;
+  static constexpr int kSmemBytes = kWarps * kRingBytes + kBarBytes + kWarps * kStages * 32 + 1024;
 };
+
+// Byte offset of 16-byte chunk `cg` (dims 8cg..8cg+7) of token `t` inside a K or V tile in
+// shared memory, as the 128-byte-swizzled TMA boxes lay it out: either two 64-dim boxes of
+// 16 rows (row t of box cg / 8), or one box of 32 128-byte rows (row 2t + cg / 8).
+template <int D>
+__device__ __forceinline__ uint32_t tile_off(int t, int cg) {
+  if constexpr (Geometry<D>::kOneBox) {
+    const int r = 2 * t + (cg >> 3);
+    return r * 128 + (((cg & 7) ^ (r & 7)) << 4);
+  } else {
+    return (cg >> 3) * 2048 + t * 128 + (((cg & 7) ^ (t & 7)) << 4);
+  }
+}
 
 struct ItemInfo {
   int b, h, part, nparts, ctx, nblk, part_global;
 };
 
+// Work item (claim order) -> (sequence, partition, KV head): one descriptor load.
 __device__ __forceinline__ ItemInfo decode_item(const DecodeArgs& a, int item) {
   ItemInfo it;
-  it.part_global = item / a.num_kv_heads;
-  it.h = item - it.part_global * a.num_kv_heads;
-  int lo = 0, hi = a.batch - 1;
-  while (lo < hi) {  // largest b with prefix[b] <= part_global
-    const int mid = (lo + hi + 1) >> 1;
-    if (__ldg(a.prefix + mid) <= it.part_global) lo = mid; else hi = mid - 1;
-  }
-  it.b = lo;
-  it.part = it.part_global - __ldg(a.prefix + lo);
-  it.nparts = __ldg(a.prefix + lo + 1) - __ldg(a.prefix + lo);
-  int ctx = __ldg(a.context_lens + lo);
-  it.ctx = ctx > a.max_blocks * kBlock ? a.max_blocks * kBlock : ctx;
-  const int total_blk = (it.ctx + kBlock - 1) / kBlock;
-  const int rem = total_blk - it.part * kPartBlocks;
+  const int pidx = item / a.num_kv_heads;
+  it.h = item - pidx * a.num_kv_heads;
+  const int4 pi = __ldg(a.part_info + pidx);
+  it.b = pi.x;
+  it.part = pi.y;
+  it.part_global = pi.z;
+  it.nparts = pi.w;
+  it.ctx = __ldg(a.part_ctx + pidx);
+  const int rem = (it.ctx + kBlock - 1) / kBlock - it.part * kPartBlocks;
   it.nblk = rem < kPartBlocks ? rem : kPartBlocks;
   return it;
 }
@@ -192,7 +275,10 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
   const int g = lane >> 2, t = lane & 3;
   uint8_t* ring = smem + warp * G::kRingBytes;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kWarps * G::kRingBytes) + warp * S;
-  int2* meta = reinterpret_cast<int2*>(smem + kWarps * G::kRingBytes + kWarps * S * 8) + warp * S;
+  // Per stage: {item, block | invalid flag, sequence, partition}, {slot partition, nparts,
+  // context length, KV head} of the item the stage belongs to.
+  int4* meta =
+      reinterpret_cast<int4*>(smem + kWarps * G::kRingBytes + G::kBarBytes) + warp * S * 2;
 
   if (lane == 0) {
     for (int s = 0; s < S; ++s) ts::mbar_init(&bars[s], 1);
@@ -206,7 +292,10 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
   // ---- producer state (warp-uniform except p_table, one table entry per lane)
   int nxt = 0;
   if (lane == 0) nxt = atomicAdd(counter, 1);
-  int p_item = -1, p_blk = 0, p_nblk = 0, p_h = 0, p_table = 0;
+  constexpr int TABW = (kPartBlocks + 31) / 32;  // table entries per lane
+  int p_item = -1, p_blk = 0, p_nblk = 0;
+  ItemInfo p_it{};
+  int p_table[TABW];
   bool p_done = false;
 
   auto produce = [&](int s) {
@@ -214,38 +303,44 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
       const int item = __shfl_sync(0xffffffffu, nxt, 0);
       if (item < total_items) {
         if (lane == 0) nxt = atomicAdd(counter, 1);
-        const ItemInfo it = decode_item(a, item);
+        p_it = decode_item(a, item);
         p_item = item;
-        p_h = it.h;
-        p_nblk = it.nblk;
+        p_nblk = p_it.nblk;
         p_blk = 0;
-        p_table = lane < it.nblk
-                      ? __ldg(a.block_tables + int64_t(it.b) * a.max_blocks +
-                              it.part * kPartBlocks + lane)
-                      : 0;
+        const int32_t* row = a.block_tables + int64_t(p_it.b) * a.max_blocks + p_it.part * kPartBlocks;
+#pragma unroll
+        for (int w = 0; w < TABW; ++w)
+          p_table[w] = lane + 32 * w < p_it.nblk ? __ldg(row + lane + 32 * w) : 0;
       } else {
         p_done = true;
       }
     }
     if (p_done) {
       if (lane == 0) {
-        meta[s] = make_int2(-1, 0);
+        meta[2 * s] = make_int4(-1, 0, 0, 0);
         ts::mbar_arrive(&bars[s]);
       }
       return;
     }
-    const int phys = __shfl_sync(0xffffffffu, p_table, p_blk);
+    const int tab = TABW == 1 || p_blk < 32 ? p_table[0] : p_table[TABW - 1];
+    const int phys = __shfl_sync(0xffffffffu, tab, p_blk & 31);
     const bool valid = phys >= 0 && int64_t(phys) < a.num_blocks;
     if (lane == 0) {
-      meta[s] = make_int2(p_item, valid ? p_blk : (p_blk | 0x40000000));
+      meta[2 * s] = make_int4(p_item, valid ? p_blk : (p_blk | 0x40000000), p_it.b, p_it.part);
+      meta[2 * s + 1] = make_int4(p_it.part_global, p_it.nparts, p_it.ctx, p_it.h);
       if (valid) {
         ts::mbar_arrive_expect_tx(&bars[s], G::kStageBytes);
-        const int row = (phys * a.num_kv_heads + p_h) * kBlock;
+        const int row = (phys * a.num_kv_heads + p_it.h) * kBlock;
         uint8_t* st = ring + s * G::kStageBytes;
+        if constexpr (G::kOneBox) {
+          ts::tma_load_2d(st, &kmap, &bars[s], 0, 2 * row);
+          ts::tma_load_2d(st + G::kTileBytes, &vmap, &bars[s], 0, 2 * row);
+        } else {
 #pragma unroll
-        for (int hf = 0; hf < G::kHalves; ++hf) {
-          ts::tma_load_2d(st + hf * 2048, &kmap, &bars[s], hf * 64, row);
-          ts::tma_load_2d(st + G::kTileBytes + hf * 2048, &vmap, &bars[s], hf * 64, row);
+          for (int hf = 0; hf < G::kHalves; ++hf) {
+            ts::tma_load_2d(st + hf * 2048, &kmap, &bars[s], hf * 64, row);
+            ts::tma_load_2d(st + G::kTileBytes + hf * 2048, &vmap, &bars[s], hf * 64, row);
+          }
         }
       } else {
         atomicExch(a.header + 1, 2);  // block id outside the pool: flagged, block skipped
@@ -265,9 +360,14 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
   float oacc[NT][MTILES][4];
   float m_run[NT][2], l_run[NT][2];
 
-  auto start_item = [&](int item) {
-    cur_item = item;
-    it = decode_item(a, item);
+  auto start_item = [&](const int4& m0, const int4& m1) {
+    cur_item = m0.x;
+    it.b = m0.z;
+    it.part = m0.w;
+    it.part_global = m1.x;
+    it.nparts = m1.y;
+    it.ctx = m1.z;
+    it.h = m1.w;
     const T* qb = static_cast<const T*>(a.query) + int64_t(it.b) * a.q_stride;
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) {
@@ -386,11 +486,11 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
       failed = true;
       break;
     }
-    const int2 md = meta[s];
+    const int4 md = meta[2 * s];
     if (md.x < 0) break;
     if (md.x != cur_item) {
       if (cur_item >= 0) finish_item();
-      start_item(md.x);
+      start_item(md, meta[2 * s + 1]);
     }
     if ((md.y & 0x40000000) == 0) {
       const uint32_t kb = ts::smem_u32(ring + s * G::kStageBytes);
@@ -408,9 +508,8 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
         const int row = (lane & 7) + ((lane >> 3) & 1) * 8;
 #pragma unroll
         for (int ks = 0; ks < KSTEPS; ++ks) {
-          const int chunk = (ks & 3) * 2 + (lane >> 4);
           uint32_t af[4];
-          ts::ldmatrix_x4(af, kb + (ks >> 2) * 2048 + row * 128 + ((chunk ^ (row & 7)) << 4));
+          ts::ldmatrix_x4(af, kb + tile_off<D>(row, ks * 2 + (lane >> 4)));
 #pragma unroll
           for (int nt = 0; nt < NT; ++nt) Mma::run(sacc[nt], af, qf[nt][ks][0], qf[nt][ks][1]);
         }
@@ -458,10 +557,8 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
         const int vtok = (lane & 7) + (lane >> 4) * 8;
 #pragma unroll
         for (int mt = 0; mt < MTILES; ++mt) {
-          const int cg = mt * 2 + ((lane >> 3) & 1);
           uint32_t af[4];
-          ts::ldmatrix_x4_trans(
-              af, vb + (cg >> 3) * 2048 + vtok * 128 + (((cg & 7) ^ (vtok & 7)) << 4));
+          ts::ldmatrix_x4_trans(af, vb + tile_off<D>(vtok, mt * 2 + ((lane >> 3) & 1)));
 #pragma unroll
           for (int nt = 0; nt < NT; ++nt) {
             Mma::run(oacc[nt][mt], af, pb[nt][0], pb[nt][1]);
@@ -519,9 +616,12 @@ int num_sms() {
 bool make_pool_map(CUtensorMap* map, const void* pool, int64_t rows, int hd, int dtype) {
   auto encode = get_encode();
   if (encode == nullptr) return false;
-  const cuuint64_t dims[2] = {cuuint64_t(hd), cuuint64_t(rows)};
-  const cuuint64_t strides[1] = {cuuint64_t(hd) * 2};
-  const cuuint32_t box[2] = {64, kBlock};
+  // One box per 4 KiB tile views each 256-byte token row as two 128-byte rows.
+  const bool one_box = TS_DECODE_ONE_BOX && hd == 128;
+  const cuuint64_t dims[2] = {one_box ? 64 : cuuint64_t(hd),
+                              one_box ? cuuint64_t(rows) * 2 : cuuint64_t(rows)};
+  const cuuint64_t strides[1] = {one_box ? 128 : cuuint64_t(hd) * 2};
+  const cuuint32_t box[2] = {64, one_box ? 2 * kBlock : cuuint32_t(kBlock)};
   const cuuint32_t estr[2] = {1, 1};
   const CUresult r = encode(
       map, dtype == TS_BFLOAT16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
@@ -637,6 +737,8 @@ extern "C" int ts_paged_decode(void* out, const void* query, int64_t query_token
   a.scale_log2 = scale * kLog2e;
   a.header = reinterpret_cast<int*>(ws);
   a.prefix = reinterpret_cast<int*>(ws + w.prefix);
+  a.part_info = reinterpret_cast<int4*>(ws + w.part_info);
+  a.part_ctx = reinterpret_cast<int*>(ws + w.part_ctx);
   a.arrive = reinterpret_cast<int*>(ws + w.arrive);
   a.part_o = reinterpret_cast<float*>(ws + w.part_o);
   a.part_ml = reinterpret_cast<float2*>(ws + w.part_ml);
@@ -761,6 +863,8 @@ extern "C" int ts_paged_decode_no_alloc(void* out, const void* query, int64_t qu
   a.scale_log2 = scale * kLog2e;
   a.header = reinterpret_cast<int*>(ws);
   a.prefix = reinterpret_cast<int*>(ws + w.prefix);
+  a.part_info = reinterpret_cast<int4*>(ws + w.part_info);
+  a.part_ctx = reinterpret_cast<int*>(ws + w.part_ctx);
   a.arrive = reinterpret_cast<int*>(ws + w.arrive);
   a.part_o = reinterpret_cast<float*>(ws + w.part_o);
   a.part_ml = reinterpret_cast<float2*>(ws + w.part_ml);
