@@ -46,7 +46,7 @@ def parse() -> argparse.Namespace:
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["cuda", "reference"], default="cuda")
-    ap.add_argument("--workload", choices=["decode", "prefill"], default="decode",
+    ap.add_argument("--workload", choices=["decode", "prefill", "decode70b"], default="decode",
                     help="decode: the headline decode-op line; prefill: chunked prefill with a "
                          "1024-token cached prefix, 32 layers")  # fmt: skip
     ap.add_argument("--layers", type=int, default=32, help="prefill workload only")
@@ -249,6 +249,9 @@ def main() -> None:
     local = int(os.environ.get("LOCAL_RANK", "0"))
     if args.workload == "prefill":
         run_prefill(args, world, rank, local)
+        return
+    if args.workload == "decode70b":
+        run_decode70b(args, world, rank, local)
         return
     if args.impl == "reference":
         if rank == 0:
@@ -474,6 +477,163 @@ def run_cuda(args: argparse.Namespace, world: int, rank: int, local: int) -> Non
                 "kind": "port",
                 "sample": f"{len(seqs)} of {B} sequences ({sb / 1e6:.0f} MB of KV) x {reps} passes",
             }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier(device_ids=[local])
+        dist.destroy_process_group()
+
+
+D70_METRIC = "KV-head-sharded paged decode KV-read GB/s (Llama-3-70B attention, 80 layers)"
+
+
+def run_decode70b(args: argparse.Namespace, world: int, rank: int, local: int) -> None:
+    """Llama-3-70B attention geometry, KV heads sharded over the ranks, 80 layers per step.
+
+    Every rank holds the pool of its Hkv/N KV heads under the replicated block tables and runs
+    K1 + K2 for its Hq/N query heads; each layer's output [B, Hq/N, D] is all-gathered over
+    NVLink on a second stream (overlapping the next layer) and re-ordered to [B, Hq, D]. The
+    80-layer KV does not fit one GPU, so the step cycles through as many resident layer pools
+    as fit; every layer still reads its full KV from HBM.
+    """
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    from tokenserve_b200 import ops
+    from tokenserve_b200.sharding import gather_heads, heads_from_gathered, shard_heads
+    from tokenserve_b200.workloads import decode70b_workload
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180), device_id=dev)
+    ops.load_library()
+    case = decode70b_workload(seed=0)  # identical tables on every rank
+    sh = shard_heads(case.num_q_heads, case.num_kv_heads, world, rank)
+    B, hq_r, hkv_r, d, nb = case.batch, sh.num_q_heads, sh.num_kv_heads, 128, case.num_blocks
+    dt = torch.bfloat16
+    layers = 80
+    per_layer = 2 * nb * hkv_r * 16 * d * 2
+    free, _ = torch.cuda.mem_get_info(dev)
+    resident = max(1, min(layers, int(0.75 * free) // per_layer))
+    g = torch.Generator(device=dev).manual_seed(3000 + rank)
+    pools = torch.empty((resident, 2, nb, hkv_r, 16, d), dtype=dt, device=dev)
+    for li in range(resident):
+        for kv in range(2):
+            pools[li, kv].normal_(0.0, 0.5, generator=g)
+    q = (torch.randn(B, hq_r, d, generator=g, device=dev) * 0.5).to(dt)
+    knew = (torch.randn(B, hkv_r, d, generator=g, device=dev) * 0.5).to(dt)
+    vnew = (torch.randn(B, hkv_r, d, generator=g, device=dev) * 0.5).to(dt)
+    slots = torch.from_numpy(case.append_slots).to(dev)
+    bt = torch.from_numpy(case.block_tables).to(dev)
+    cl = torch.from_numpy(case.context_lens).to(dev)
+    nbuf = 4  # output ring: layer li's gather may lag the decode of li+1..li+3
+    outs = [torch.empty(B, hq_r, d, dtype=dt, device=dev) for _ in range(nbuf)]
+    gath = [torch.empty(world, B, hq_r, d, dtype=dt, device=dev) for _ in range(nbuf)]
+    full = [torch.empty(B, world * hq_r, d, dtype=dt, device=dev) for _ in range(nbuf)]
+    ws = torch.empty(ops.decode_workspace_size(B, hq_r, hkv_r, d, bt.shape[1], 16, dt),
+                     dtype=torch.uint8, device=dev)  # fmt: skip
+    comp = torch.cuda.current_stream()
+    comm = torch.cuda.Stream(device=dev)
+    made = [torch.cuda.Event() for _ in range(nbuf)]
+    freed = [torch.cuda.Event() for _ in range(nbuf)]
+    kv_bytes_rank = case.kv_bytes(2) * hkv_r // case.num_kv_heads
+
+    def step(dec_ev=None, ag_ev=None) -> None:  # type: ignore[no-untyped-def]
+        for li in range(layers):
+            p = li % nbuf
+            pool = pools[li % resident]
+            if li >= nbuf and world > 1:
+                comp.wait_event(freed[p])  # the gather of layer li-nbuf has read outs[p]
+            ops.reshape_and_cache(knew, vnew, pool[0], pool[1], slots)
+            if dec_ev is not None:
+                dec_ev[li][0].record(comp)
+            ops.paged_decode(outs[p], q, pool[0], pool[1], bt, cl, d**-0.5, ws)
+            if dec_ev is not None:
+                dec_ev[li][1].record(comp)
+            if world > 1:
+                made[p].record(comp)
+                with torch.cuda.stream(comm):
+                    comm.wait_event(made[p])
+                    if ag_ev is not None:
+                        ag_ev[li][0].record(comm)
+                    gather_heads(outs[p], gath[p])
+                    if ag_ev is not None:
+                        ag_ev[li][1].record(comm)
+                    full[p].copy_(heads_from_gathered(gath[p]))
+                    freed[p].record(comm)
+        if world > 1:
+            comp.wait_stream(comm)
+
+    def barrier() -> None:
+        if world > 1:
+            dist.barrier(device_ids=[local])
+        torch.cuda.synchronize()
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    barrier()
+    mk = lambda: [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))  # noqa: E731
+                  for _ in range(layers)]  # fmt: skip
+    dec_ev = [mk() for _ in range(args.steps)]
+    ag_ev = [mk() for _ in range(args.steps)]
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(dev) as clocks:
+        e0.record(comp)
+        for i in range(args.steps):
+            step(dec_ev[i], ag_ev[i])
+        e1.record(comp)
+        torch.cuda.synchronize()
+    barrier()
+    elapsed = e0.elapsed_time(e1) / 1e3
+    dec_t = sum(a.elapsed_time(b) for st in dec_ev for a, b in st) / 1e3 / (args.steps * layers)
+    ag_t = (sum(a.elapsed_time(b) for st in ag_ev for a, b in st) / 1e3 / (args.steps * layers)
+            if world > 1 else 0.0)  # fmt: skip
+    stats = torch.tensor([elapsed, dec_t, ag_t], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(stats, op=dist.ReduceOp.MAX)
+    elapsed, dec_t, ag_t = stats.tolist()
+    if rank == 0:
+        peak, peak_kind = peaks()
+        total_kv = kv_bytes_rank * world * layers * args.steps
+        ag_bytes = B * case.num_q_heads * d * 2
+        line = {
+            "metric": D70_METRIC,
+            "value": round(total_kv / elapsed / 1e9, 1),
+            "unit": "GB/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": max(args.warmup, 3),
+            "ms_per_step": round(1000 * elapsed / args.steps, 3),
+            "higher_is_better": True,
+            "scaling": "strong",
+            "vs_baseline": None,
+            "dtype": "bf16",
+            "data": "synthetic",
+            "config": {
+                "workload": "Llama-3-70B attention decode (64q/8kv, D=128, bf16, block 16), "
+                            "80 layers, KV heads sharded over ranks",
+                "batch_admitted": B, "batch_requested": 512,
+                "context": "log-normal median 4096 sigma 1.0 clipped 16..32768",
+                "pool_blocks": nb, "pool": "85% of the batch's demand; sequences past it wait",
+                "resident_layer_pools_per_rank": resident,
+                "parallelism": f"KV-head sharding x{world} (Hkv/N={hkv_r}, Hq/N={hq_r})",
+                "collective": "per-layer all_gather of [B, Hq/N, D] on a second stream" if world > 1 else "none",
+            },
+            "per_rank_frac_of_hbm_peak": round(kv_bytes_rank * layers * args.steps / elapsed / 1e9 / peak, 4),
+            "roofline": {
+                "bound": "hbm", "kernel": "paged_decode_kernel",
+                "achieved": round((kv_bytes_rank + 2 * B * hq_r * d * 2) / dec_t / 1e9, 1),
+                "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",
+                "frac": round((kv_bytes_rank + 2 * B * hq_r * d * 2) / dec_t / 1e9 / peak, 4),
+                "avg_launch_us": round(dec_t * 1e6, 2),
+            },
+            "allgather": ({"bytes_per_layer": ag_bytes, "avg_us": round(ag_t * 1e6, 2),
+                           "algbw_gbs": round(ag_bytes / ag_t / 1e9, 1)} if world > 1 else None),
+            "gpu_launches": (3 * layers + (2 if world > 1 else 0) * layers) * args.steps,
+            "clocks": clocks.summary(),
+        }  # fmt: skip
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier(device_ids=[local])

@@ -9,6 +9,10 @@
   sequences share one seeded 1024-token prefix already resident as cached blocks, each has a
   unique suffix of uniform 256..2048 tokens, processed in 512-token chunks that attend causally
   over the cached prefix plus the chunk itself.
+* :func:`decode70b_workload` — decode at Llama-3-70B attention geometry (64 query / 8 KV heads,
+  head_dim 128, bf16, block 16): 512 sequences with log-normal contexts (median 4096, sigma 1.0,
+  clipped to 16..32768) against a pool sized to 85% of their demand; the sequences admitted are
+  the longest prefix of the batch whose blocks fit, the rest wait (preempted).
 * :func:`small_paged_case` — the same construction at sizes a CPU oracle checks in seconds.
 
 Only numpy is used for the index arithmetic, so the same seed gives the same tables on every
@@ -170,3 +174,15 @@ def prefill_workload(seed: int = 0, num_seqs: int = 64, prefix: int = 1024, chun
             slots.append(tables[s][pos // bs].astype(np.int64) * bs + pos % bs)
         rounds.append(PrefillRound(seqs, c, ctx, qsl, bt, np.concatenate(slots)))
     return PrefillWorkload(num_blocks, bs, 32, 8, 128, num_layers, suffix, rounds)
+
+
+def decode70b_workload(seed: int = 0, batch: int = 512, undersize: float = 0.85) -> PagedCase:
+    """The Llama-3-70B decode workload (see module docstring); returns the admitted batch."""
+    rng = np.random.default_rng(seed)
+    ctx = lognormal_context_lens(rng, batch, 4096.0, 1.0, 16, 32768)
+    need = (ctx.astype(np.int64) + 15) // 16
+    num_blocks = int(undersize * need.sum())
+    admitted = int(np.searchsorted(np.cumsum(need), num_blocks, side="right"))
+    ctx = ctx[:admitted]
+    tables = tables_from_permutation(rng, ctx, num_blocks, 16)
+    return PagedCase(num_blocks, 16, 64, 8, 128, ctx, tables, seed)
