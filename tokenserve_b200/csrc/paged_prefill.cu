@@ -7,16 +7,18 @@
 // sequence whose step ends at context_lens[s] sits at position context_lens[s] - q_len + j.
 //
 // bf16/fp16, head_dim 128, block 16, G = Hq/Hkv in {1,2,4,8,16}: tcgen05 tensor-core kernel.
-//   * CTA = (sequence, KV head, query tile). The tile's 128 rows are 128/G query tokens x the
-//     G query heads of the KV head (GQA packing), so each K/V tile feeds all G heads.
-//   * warp 4 (producer): Q tile by one 3-D TMA box per 64-column half, then K/V tiles of 128
+//   * CTA = (sequence, KV head, pair of query tiles). A tile's 128 rows are 128/G query tokens x
+//     the G query heads of the KV head (GQA packing), so each K/V tile feeds all G heads, and
+//     both tiles of the pair share every K/V tile they need.
+//   * warp 8 (producer): Q tiles by one 3-D TMA box per 64-column half, then K/V tiles of 128
 //     tokens (8 blocks, gathered through the block table with 2-D TMA boxes, 128-byte swizzle,
 //     no multicast) into a 2-stage ring.
-//   * warp 5 (one lane): tcgen05.mma S = Q K^T (M=N=K=128, both K-major) into one of two TMEM
-//     S buffers, then O += P V with P read from TMEM (bf16, written over S) and V MN-major.
-//     QK of tile j+1 is issued before PV of tile j so it overlaps the softmax of tile j.
-//   * warps 0-3 (128 threads, thread = row = TMEM lane): online softmax in fp32 (exp2 domain)
-//     with the causal mask, P back to TMEM, O rescale in TMEM, and the epilogue.
+//   * warp 9 (one lane): tcgen05.mma S_x = Q_x K^T (M=N=K=128, both K-major) into tile x's TMEM
+//     S, then O_x += P_x V with P read from TMEM (bf16, written over S) and V MN-major, in the
+//     order PV_A(j), QK_A(j+1), PV_B(j), QK_B(j+1): one tile's softmax overlaps the other's MMAs.
+//   * warps 0-3 / 4-7 (one warpgroup per query tile, thread = row = TMEM lane): online softmax
+//     in fp32 (exp2 domain, causal mask only on diagonal tiles, stale max kept unless exceeded by
+//     2^8 so O is rarely rescaled), P back to TMEM, O rescale in TMEM, and the epilogue.
 // Other shapes and fp32 use the CUDA-core kernel in attention_portable.cu.
 #include <cuda.h>
 #include <cudaTypedefs.h>
@@ -41,10 +43,16 @@ constexpr int kKvTile = 128;                 // KV tokens per tile (N of QK, K o
 constexpr int kBlock = 16;                   // tokens per KV block
 constexpr int kHalfBytes = 128 * 128;        // 128 rows x 128 bytes (64 columns)
 constexpr int kTileBytes = 2 * kHalfBytes;   // 128 x 128 16-bit elements
-constexpr int kSmemBytes = 5 * kTileBytes + 256 + 1024;
-constexpr int kThreads = 192;
+constexpr int kQTiles = 2;                   // query tiles per CTA (ping-pong)
+constexpr int kSmemBytes = (kQTiles + 4) * kTileBytes + 256 + 1024;
+// Warps 0..4*kQTiles-1: softmax, one warpgroup per query tile; then the producer and the MMA
+// warp. With 10 warps one SM sub-partition hosts 3 of them, so a thread may use at most
+// 16384 / 96 = 170 registers: the kernel is capped at 168.
+constexpr int kThreads = 32 * (4 * kQTiles + 2);
+constexpr int kMaxRegs = 168;
 constexpr float kLog2e = 1.4426950408889634f;
-constexpr uint32_t kTmemCols = 512;  // S0 [0,128), S1 [128,256), O [256,384)
+constexpr float kRescaleSlack = 8.f;  // keep a stale row max unless exceeded by 2^8
+constexpr uint32_t kTmemCols = 512;  // S_A [0,128), S_B [128,256), O_A [256,384), O_B [384,512)
 
 struct PrefillArgs {
   void* out;
@@ -60,7 +68,8 @@ struct PrefillArgs {
 };
 
 struct Bars {
-  uint64_t q_full, k_full[2], v_full[2], kv_empty[2], s_full[2], p_full[2], pv_done;
+  uint64_t q_full, k_full[2], v_full[2], kv_empty[2];
+  uint64_t s_full[kQTiles], p_full[kQTiles], pv_done[kQTiles];
   uint32_t tmem;
   int abort;
 };
@@ -75,33 +84,52 @@ __device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t phase, volatile
   return false;
 }
 
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 template <bool BF16>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __maxnreg__(kMaxRegs)
     paged_prefill_tc_kernel(const __grid_constant__ CUtensorMap qmap,
                             const __grid_constant__ CUtensorMap kmap,
                             const __grid_constant__ CUtensorMap vmap, const PrefillArgs a) {
   using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
   using Mma = ts::MmaOp<T>;
-  const int tile = blockIdx.x, h = blockIdx.y, seq = blockIdx.z;
+  const int pair = blockIdx.x, h = blockIdx.y, seq = blockIdx.z;
   const int q0 = a.qsl[seq];
   const int q_len = a.qsl[seq + 1] - q0;
-  if (tile * a.tq >= q_len) return;
+  const int tile0 = pair * kQTiles;  // query tiles tile0 (A) and tile0 + 1 (B)
+  if (tile0 * a.tq >= q_len) return;
   int ctx = a.context_lens[seq];
   if (ctx > a.max_blocks * kBlock) ctx = a.max_blocks * kBlock;
   const int p0 = ctx - q_len;
   if (p0 < 0) return;
-  const int last_q = min(q_len, (tile + 1) * a.tq) - 1;
-  const int n_kv = p0 + last_q + 1;  // keys this tile can see
-  const int n_tiles = (n_kv + kKvTile - 1) / kKvTile;
-  const int total_blk = (n_kv + kBlock - 1) / kBlock;
+  // KV tiles each query tile needs (causal), 0 for an empty tile.
+  int n_t[kQTiles];
+  int n_kv_max = 0;
+#pragma unroll
+  for (int x = 0; x < kQTiles; ++x) {
+    const int first = (tile0 + x) * a.tq;
+    if (first >= q_len) {
+      n_t[x] = 0;
+    } else {
+      const int n_kv = p0 + min(q_len, first + a.tq);
+      n_t[x] = (n_kv + kKvTile - 1) / kKvTile;
+      n_kv_max = max(n_kv_max, n_kv);
+    }
+  }
+  const int n_max = (n_kv_max + kKvTile - 1) / kKvTile;
+  const int total_blk = (n_kv_max + kBlock - 1) / kBlock;
 
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = ts::smem_u32(smem_raw);
   uint8_t* smem = smem_raw + (((raw + 1023) & ~1023u) - raw);
-  uint8_t* sQ = smem;
-  auto sK = [&](int st) { return smem + kTileBytes + st * 2 * kTileBytes; };
-  auto sV = [&](int st) { return smem + 2 * kTileBytes + st * 2 * kTileBytes; };
-  Bars* bars = reinterpret_cast<Bars*>(smem + 5 * kTileBytes);
+  auto sQ = [&](int x) { return smem + x * kTileBytes; };
+  auto sK = [&](int st) { return smem + (kQTiles + 2 * st) * kTileBytes; };
+  auto sV = [&](int st) { return smem + (kQTiles + 2 * st + 1) * kTileBytes; };
+  Bars* bars = reinterpret_cast<Bars*>(smem + (kQTiles + 4) * kTileBytes);
   volatile int* abort = &bars->abort;
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
@@ -111,10 +139,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       ts::mbar_init(&bars->k_full[i], 1);
       ts::mbar_init(&bars->v_full[i], 1);
       ts::mbar_init(&bars->kv_empty[i], 1);
-      ts::mbar_init(&bars->s_full[i], 1);
-      ts::mbar_init(&bars->p_full[i], 128);
     }
-    ts::mbar_init(&bars->pv_done, 1);
+    for (int x = 0; x < kQTiles; ++x) {
+      ts::mbar_init(&bars->s_full[x], 1);
+      ts::mbar_init(&bars->p_full[x], 128);
+      ts::mbar_init(&bars->pv_done[x], 1);
+    }
     bars->abort = 0;
     ts::fence_mbar_init();
   }
@@ -127,17 +157,20 @@ __global__ void __launch_bounds__(kThreads, 1)
   ts::tc::fence_after_sync();
   const uint32_t tmem = bars->tmem;
   const int G = a.group;
+  const int producer_warp = 4 * kQTiles, mma_warp = 4 * kQTiles + 1;
 
-  if (warp == 4) {
+  if (warp == producer_warp) {
     // ------------------------------------------------------------ producer (TMA)
     const int32_t* table = a.block_tables + int64_t(seq) * a.max_blocks;
     if (lane == 0) {
-      ts::mbar_arrive_expect_tx(&bars->q_full, kTileBytes);
-      ts::tc::tma_load_3d(sQ, &qmap, &bars->q_full, 0, h * G, q0 + tile * a.tq);
-      ts::tc::tma_load_3d(sQ + kHalfBytes, &qmap, &bars->q_full, 64, h * G, q0 + tile * a.tq);
+      ts::mbar_arrive_expect_tx(&bars->q_full, kQTiles * kTileBytes);
+      for (int x = 0; x < kQTiles; ++x)
+        for (int hf = 0; hf < 2; ++hf)
+          ts::tc::tma_load_3d(sQ(x) + hf * kHalfBytes, &qmap, &bars->q_full, hf * 64, h * G,
+                              q0 + (tile0 + x) * a.tq);
     }
     int issued = 0;
-    for (int j = 0; j < n_tiles; ++j) {
+    for (int j = 0; j < n_max; ++j) {
       const int st = j & 1;
       if (j >= 2 && !wait_bar(&bars->kv_empty[st], ((j - 2) >> 1) & 1, abort)) break;
       const int blk0 = j * (kKvTile / kBlock);
@@ -169,92 +202,132 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       ts::mbar_wait_bounded(&bars->q_full, 0);
     }
-  } else if (warp == 5) {
+  } else if (warp == mma_warp) {
     // ------------------------------------------------------------ MMA issuer (one lane)
+    // Order per KV tile j: PV_A(j), QK_A(j+1), PV_B(j), QK_B(j+1), so the softmax of one query
+    // tile overlaps the tensor-core work of the other.
     if (lane == 0) {
       constexpr uint32_t idesc_qk = ts::tc::idesc_f16(BF16, kRows, kKvTile, false);
       constexpr uint32_t idesc_pv = ts::tc::idesc_f16(BF16, kRows, 128, true);
-      const uint32_t q_addr = ts::smem_u32(sQ);
-      int last_pv = -1;
-      auto issue_qk = [&](int j) -> bool {
+      int last_pv[kQTiles];
+      for (int x = 0; x < kQTiles; ++x) last_pv[x] = -1;
+      auto issue_qk = [&](int x, int j) -> bool {
         const int st = j & 1;
         if (!wait_bar(&bars->k_full[st], (j >> 1) & 1, abort)) return false;
         ts::tc::fence_after_sync();
-        const uint32_t k_addr = ts::smem_u32(sK(st));
+        const uint32_t q_addr = ts::smem_u32(sQ(x)), k_addr = ts::smem_u32(sK(st));
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
           const uint32_t off = (kk >> 2) * kHalfBytes + (kk & 3) * 32;
-          ts::tc::mma_ss(tmem + st * 128, ts::tc::smem_desc_sw128(q_addr + off, 16, 1024),
+          ts::tc::mma_ss(tmem + x * 128, ts::tc::smem_desc_sw128(q_addr + off, 16, 1024),
                          ts::tc::smem_desc_sw128(k_addr + off, 16, 1024), idesc_qk, kk > 0);
         }
-        ts::tc::commit(&bars->s_full[st]);
+        ts::tc::commit(&bars->s_full[x]);
         return true;
       };
-      bool ok = wait_bar(&bars->q_full, 0, abort) && issue_qk(0);
-      for (int j = 0; ok && j < n_tiles; ++j) {
-        if (j + 1 < n_tiles && !issue_qk(j + 1)) break;
+      bool ok = wait_bar(&bars->q_full, 0, abort);
+      for (int x = 0; ok && x < kQTiles; ++x)
+        if (n_t[x] > 0) ok = issue_qk(x, 0);
+      for (int j = 0; ok && j < n_max; ++j) {
         const int st = j & 1;
-        if (!wait_bar(&bars->p_full[st], (j >> 1) & 1, abort) ||
-            !wait_bar(&bars->v_full[st], (j >> 1) & 1, abort))
-          break;
-        ts::tc::fence_after_sync();
-        const uint32_t v_addr = ts::smem_u32(sV(st));
+        for (int x = 0; ok && x < kQTiles; ++x) {
+          if (j >= n_t[x]) continue;
+          if (!wait_bar(&bars->p_full[x], j & 1, abort) ||
+              !wait_bar(&bars->v_full[st], (j >> 1) & 1, abort)) {
+            ok = false;
+            break;
+          }
+          ts::tc::fence_after_sync();
+          const uint32_t v_addr = ts::smem_u32(sV(st));
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk)
-          ts::tc::mma_ts(tmem + 256, tmem + st * 128 + kk * 8,
-                         ts::tc::smem_desc_sw128(v_addr + kk * 2048, kHalfBytes, 1024), idesc_pv,
-                         j > 0 || kk > 0);
-        ts::tc::commit(&bars->pv_done);
-        if (j + 2 < n_tiles) ts::tc::commit(&bars->kv_empty[st]);
-        last_pv = j;
+          for (int kk = 0; kk < 8; ++kk)
+            ts::tc::mma_ts(tmem + 256 + x * 128, tmem + x * 128 + kk * 8,
+                           ts::tc::smem_desc_sw128(v_addr + kk * 2048, kHalfBytes, 1024),
+                           idesc_pv, j > 0 || kk > 0);
+          ts::tc::commit(&bars->pv_done[x]);
+          last_pv[x] = j;
+          if (j + 1 < n_t[x] && !issue_qk(x, j + 1)) ok = false;
+        }
+        if (ok && j + 2 < n_max) ts::tc::commit(&bars->kv_empty[st]);
       }
-      if (*abort && last_pv >= 0) ts::mbar_wait_bounded(&bars->pv_done, last_pv & 1);
+      if (*abort)
+        for (int x = 0; x < kQTiles; ++x)
+          if (last_pv[x] >= 0) ts::mbar_wait_bounded(&bars->pv_done[x], last_pv[x] & 1);
     }
-  } else {
+  } else if (warp < 4 * kQTiles) {
     // ------------------------------------------------------------ softmax / epilogue
-    const int r = threadIdx.x;  // tile row == TMEM lane
+    const int x = warp / 4;                 // query tile of this warpgroup
+    const int r = threadIdx.x - 128 * x;    // tile row == TMEM lane
+    const int n_x = n_t[x];
     const int i = r / G, g = r - (r / G) * G;
-    const int qi = tile * a.tq + i;
+    const int qi = (tile0 + x) * a.tq + i;
     const bool row_valid = qi < q_len;
     const int pos = p0 + (row_valid ? qi : q_len - 1);
-    const uint32_t lane_base = tmem + (uint32_t(warp * 32) << 16);
+    const uint32_t lane_base = tmem + (uint32_t((warp & 3) * 32) << 16);
+    const uint32_t s_col = x * 128, o_col = 256 + x * 128;
+    // The first query tile to use the CTA's last KV tile clears its rows past the last key.
+    int zero_tile = -1;
+    for (int y = kQTiles - 1; y >= 0; --y)
+      if (n_t[y] == n_max) zero_tile = y;
+    const float sl = a.scale_log2;
     float m_run = -INFINITY, l_run = 0.f;
-    bool ok = true;
-    for (int j = 0; j < n_tiles; ++j) {
+    bool ok = n_x > 0;
+    for (int j = 0; ok && j < n_x; ++j) {
       const int st = j & 1;
-      if (!wait_bar(&bars->s_full[st], (j >> 1) & 1, abort)) {
+      if (!wait_bar(&bars->s_full[x], j & 1, abort)) {
         ok = false;
         break;
       }
       ts::tc::fence_after_sync();
-      float s[128];
+      const int limit = pos - j * kKvTile;  // columns c <= limit are visible
+      const bool full_tile = limit >= kKvTile - 1;
+      // Pass 1: row max, 32 columns at a time.
+      float mx = -INFINITY;
 #pragma unroll
       for (int c4 = 0; c4 < 4; ++c4) {
         uint32_t rr[32];
-        ts::tc::tmem_ld32(lane_base + st * 128 + c4 * 32, rr);
+        ts::tc::tmem_ld32(lane_base + s_col + c4 * 32, rr);
         ts::tc::wait_ld();
 #pragma unroll
-        for (int c = 0; c < 32; ++c) s[c4 * 32 + c] = __uint_as_float(rr[c]);
+        for (int c = 0; c < 32; ++c) {
+          const float v = __uint_as_float(rr[c]);
+          mx = fmaxf(mx, full_tile || c4 * 32 + c <= limit ? v : -INFINITY);
+        }
       }
-      const int limit = pos - j * kKvTile;  // columns c <= limit are visible
-      float mx = -INFINITY;
+      // Lazy rescaling: a stale max is kept while the new one stays within 2^8 of it.
+      const float m_tile = mx * sl;
+      float corr = 1.f;
+      if (m_tile > m_run + kRescaleSlack) {
+        corr = ex2(m_run - m_tile);
+        m_run = m_tile;
+      }
+      // Pass 2: P = exp2(s * scale - m), written back over the columns already read.
+      float sum0 = 0.f, sum1 = 0.f;
 #pragma unroll
-      for (int c = 0; c < 128; ++c) {
-        s[c] = c <= limit ? s[c] * a.scale_log2 : -INFINITY;
-        mx = fmaxf(mx, s[c]);
-      }
-      const float m_new = fmaxf(m_run, mx);
-      const float corr = exp2f(m_run - m_new);
-      float sum = 0.f;
+      for (int c4 = 0; c4 < 4; ++c4) {
+        uint32_t rr[32];
+        ts::tc::tmem_ld32(lane_base + s_col + c4 * 32, rr);
+        ts::tc::wait_ld();
+        uint32_t pk[16];
 #pragma unroll
-      for (int c = 0; c < 128; ++c) {
-        s[c] = exp2f(s[c] - m_new);
-        sum += s[c];
+        for (int c = 0; c < 32; c += 2) {
+          const int col = c4 * 32 + c;
+          float p0 = ex2(fmaf(__uint_as_float(rr[c]), sl, -m_run));
+          float p1 = ex2(fmaf(__uint_as_float(rr[c + 1]), sl, -m_run));
+          if (!full_tile) {
+            p0 = col <= limit ? p0 : 0.f;
+            p1 = col + 1 <= limit ? p1 : 0.f;
+          }
+          sum0 += p0;
+          sum1 += p1;
+          pk[c / 2] = Mma::pack(p0, p1);
+        }
+        ts::tc::tmem_st16(lane_base + s_col + c4 * 16, pk);
       }
-      l_run = l_run * corr + sum;
-      m_run = m_new;
+      ts::tc::wait_st();
+      l_run = l_run * corr + (sum0 + sum1);
       if (j > 0) {
-        if (!wait_bar(&bars->pv_done, (j - 1) & 1, abort)) {
+        if (!wait_bar(&bars->pv_done[x], (j - 1) & 1, abort)) {
           ok = false;
           break;
         }
@@ -263,30 +336,23 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int c4 = 0; c4 < 4; ++c4) {
             uint32_t rr[32];
-            ts::tc::tmem_ld32(lane_base + 256 + c4 * 32, rr);
+            ts::tc::tmem_ld32(lane_base + o_col + c4 * 32, rr);
             ts::tc::wait_ld();
 #pragma unroll
             for (int c = 0; c < 32; ++c) rr[c] = __float_as_uint(__uint_as_float(rr[c]) * corr);
-            ts::tc::tmem_st32(lane_base + 256 + c4 * 32, rr);
+            ts::tc::tmem_st32(lane_base + o_col + c4 * 32, rr);
           }
+          ts::tc::wait_st();
         }
       }
-#pragma unroll
-      for (int hf = 0; hf < 2; ++hf) {
-        uint32_t pk[32];
-#pragma unroll
-        for (int c = 0; c < 32; ++c) pk[c] = Mma::pack(s[64 * hf + 2 * c], s[64 * hf + 2 * c + 1]);
-        ts::tc::tmem_st32(lane_base + st * 128 + 32 * hf, pk);
-      }
-      ts::tc::wait_st();
-      if (j * kKvTile + kKvTile > n_kv) {
+      if (x == zero_tile && j == n_max - 1 && j * kKvTile + kKvTile > n_kv_max) {
         // Rows past the last visible key hold stale or unwritten data: zero them so that
         // P = 0 times V stays 0.
         if (!wait_bar(&bars->v_full[st], (j >> 1) & 1, abort)) {
           ok = false;
           break;
         }
-        if (j * kKvTile + r >= n_kv) {
+        if (j * kKvTile + r >= n_kv_max) {
           uint4* v0 = reinterpret_cast<uint4*>(sV(st) + r * 128);
           uint4* v1 = reinterpret_cast<uint4*>(sV(st) + kHalfBytes + r * 128);
 #pragma unroll
@@ -295,9 +361,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         ts::fence_proxy_async_smem();
       }
       ts::tc::fence_before_sync();
-      ts::mbar_arrive(&bars->p_full[st]);
+      ts::mbar_arrive(&bars->p_full[x]);
     }
-    if (ok && wait_bar(&bars->pv_done, (n_tiles - 1) & 1, abort)) {
+    if (ok && wait_bar(&bars->pv_done[x], (n_x - 1) & 1, abort)) {
       ts::tc::fence_after_sync();
       const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
       T* orow = static_cast<T*>(a.out) +
@@ -305,7 +371,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
       for (int c4 = 0; c4 < 4; ++c4) {
         uint32_t rr[32];
-        ts::tc::tmem_ld32(lane_base + 256 + c4 * 32, rr);
+        ts::tc::tmem_ld32(lane_base + o_col + c4 * 32, rr);
         ts::tc::wait_ld();
         uint32_t pk[16];
 #pragma unroll
@@ -441,15 +507,9 @@ extern "C" int ts_paged_prefill(void* out, const void* query, int64_t query_toke
   a.scale_log2 = scale * kLog2e;
   const int tiles = (max_query_len + a.tq - 1) / a.tq;
   if (tiles == 0) return ts::ok();
-  dim3 grid(tiles, num_kv_heads, num_seqs);
-  if (dtype == TS_BFLOAT16) {
-    auto kern = paged_prefill_tc_kernel<true>;
-    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
-    kern<<<grid, kThreads, kSmemBytes, s>>>(qm, km, vm, a);
-  } else {
-    auto kern = paged_prefill_tc_kernel<false>;
-    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
-    kern<<<grid, kThreads, kSmemBytes, s>>>(qm, km, vm, a);
-  }
+  dim3 grid((tiles + kQTiles - 1) / kQTiles, num_kv_heads, num_seqs);
+  auto kern = dtype == TS_BFLOAT16 ? paged_prefill_tc_kernel<true> : paged_prefill_tc_kernel<false>;
+  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+  kern<<<grid, kThreads, kSmemBytes, s>>>(qm, km, vm, a);
   return ts::launch_status("paged_prefill");
 }
