@@ -14,6 +14,13 @@ It writes:
   and the backend's final shadow-KV array (simulated.py:101,147-169).
 * ``eager_attention.npz`` — transformers 5.5.0 ``eager_attention_forward``
   (models/llama/modeling_llama.py:199) on seeded decode and causal-prefill inputs (float32).
+* ``llama8b_engine_trace.json.gz`` — the Llama-3-8B engine workload's batch stream: tokenserve's
+  Engine (block 16, a pool of 51,500 blocks = 60% of a B200's HBM at 2 MiB per block for 32
+  layers) serving 160 requests arriving Poisson at 20 req/s with prompt ids uniform over 128256,
+  prompt lengths uniform 128..2048, 30% sharing a seeded 512-token prefix, greedy output lengths
+  uniform 64..512 (ignore_eos), driven by SimulatedBackend with a 25 ms modelled step. Stored
+  compactly: each sequence's token ids and block table, and per step the items'
+  (seq, start, n, sample, table length).
 * ``tiny_llama_trace.json.gz`` — the tiny-Llama engine workload (2 layers, hidden 256, 4 q / 2 kv
   heads, head_dim 64, rope theta 1e4, vocab 32000, fp32, torch seed 0; block 16 x 512 blocks;
   32 requests with prompt ids uniform in [3, 32000), lengths uniform 64..512, half sharing one
@@ -303,7 +310,77 @@ def make_tiny_llama_trace() -> None:
           f"preemptions {preempt}, min margin {min(oracle.margins):.3e}")
 
 
+def make_llama8b_engine_trace() -> None:
+    rng = np.random.default_rng(4)
+    n = 160
+    prefix = rng.integers(0, 128256, 512).tolist()
+    prompts, params = [], []
+    for i in range(n):
+        p = rng.integers(0, 128256, int(rng.integers(128, 2049))).tolist()
+        if rng.random() < 0.3:
+            p[:512] = prefix
+        prompts.append(p)
+        params.append(SamplingParams(max_tokens=int(rng.integers(64, 513)), ignore_eos=True))
+    arrivals = np.cumsum(rng.exponential(1 / 20.0, n)).tolist()
+    tok = ByteTokenizer()
+    nb = 51500
+    backend = SimulatedBackend(SimulatedBackendConfig(0, 0), block_size=16, num_blocks=nb,
+                               eos_token_id=tok.eos_token_id)  # fmt: skip
+    steps: list[list[list[int]]] = []
+    tables: dict[int, list[int]] = {}
+    tokens: dict[int, list[int]] = {}
+
+    class Compact(Backend):
+        name = "simulated"
+        supports_prefix_caching = True
+
+        async def execute(self, batch):  # type: ignore[no-untyped-def]
+            rows = []
+            for it in batch:
+                t = list(it.block_table)
+                old = tables.get(it.seq_id)
+                if old is not None and t[: len(old)] != old[: len(t)]:
+                    raise AssertionError("block table changed in place (preemption): not compactable")
+                if old is None or len(t) > len(old):
+                    tables[it.seq_id] = t
+                tokens[it.seq_id] = list(it.token_ids[: it.end])
+                rows.append([it.seq_id, it.start, it.num_new_tokens, int(it.sample), len(t),
+                             it.num_prompt_tokens])  # fmt: skip
+            steps.append(rows)
+            return await backend.execute(batch)
+
+    clock = VirtualClock()
+    eng = Engine(EngineConfig(block_size=16, num_blocks=nb), Compact(), tok, clock=clock)
+
+    async def run() -> None:
+        nxt = 0
+        while nxt < n or eng.scheduler.has_unfinished():
+            while nxt < n and arrivals[nxt] <= clock.t:
+                eng.add_request(f"r{nxt}", prompts[nxt], params[nxt])
+                nxt += 1
+            if eng.scheduler.has_unfinished():
+                await eng.step()
+                clock.t += 0.025
+            else:
+                clock.t = arrivals[nxt]
+
+    asyncio.run(run())
+    dump_gz(HERE / "llama8b_engine_trace.json.gz", {
+        "block_size": 16, "num_blocks": nb, "steps": steps,
+        "tables": {str(k): v for k, v in tables.items()},
+        "tokens": {str(k): v for k, v in tokens.items()},
+        "prefix_hit_tokens": eng.scheduler.prefix_hit_tokens,
+        "preemptions": eng.scheduler.num_preemptions,
+    })  # fmt: skip
+    print(f"llama8b trace: {len(steps)} steps, prefix hits {eng.scheduler.prefix_hit_tokens}")
+
+
 if __name__ == "__main__":
+    if len(sys.argv) > 1:
+        for name in sys.argv[1:]:
+            globals()[f"make_{name}"]()
+        raise SystemExit(0)
+    make_llama8b_engine_trace()
     make_slot_mapping()
     make_sim_trace()
     make_eager_attention()

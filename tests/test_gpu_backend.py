@@ -22,6 +22,7 @@ import torch
 
 from tests.conftest import GOLDEN
 from tokenserve_b200.backend import CudaPagedBackend, CudaPagedBackendConfig
+from tokenserve_b200 import replay
 from tokenserve_b200.interface import BatchItem, KVCorruptionError
 
 pytestmark = pytest.mark.gpu
@@ -44,13 +45,7 @@ def llama(vocab: int, seed: int = 0, **over) -> torch.nn.Module:  # type: ignore
 
 
 def batches(trace: dict):  # type: ignore[no-untyped-def]
-    tokens = {int(k): v for k, v in trace["tokens"].items()}
-    for step in trace["steps"]:
-        yield [
-            BatchItem(seq_id=r[0], token_ids=tokens[r[0]], start=r[1], num_new_tokens=r[2],
-                      num_prompt_tokens=r[3], block_table=r[6], sample=bool(r[4]), seed=r[5])
-            for r in step["items"]
-        ], {int(k): v for k, v in step["sampled"].items()}  # fmt: skip
+    yield from replay.steps(trace)
 
 
 def test_greedy_tokens_identical_to_reference_on_tiny_llama_trace(cuda_device) -> None:  # type: ignore[no-untyped-def]
