@@ -695,16 +695,29 @@ def run_engine(args: argparse.Namespace, local: int) -> None:
     steps = list(replay.steps(trace))
     n_sampled = sum(it.sample for b, _ in steps for it in b)
     n_tokens = sum(it.num_new_tokens for b, _ in steps for it in b)
-    for b, _ in steps[:20]:
+    # Warm-up: one untimed replay (captures the decode-step CUDA graphs, as a server would at
+    # start-up, and settles cuBLAS plans).
+    t_w = time.perf_counter()
+    for b, _ in steps:
         backend._execute(b)
     torch.cuda.synchronize()
+    warm_s = time.perf_counter() - t_w
     mismatches = 0
     replays = max(1, args.replays)
+    t_dec = t_mix = 0.0
+    n_dec = 0
     with ClockSampler(dev) as clocks:
         t0 = time.perf_counter()
         for _ in range(replays):
             for b, want in steps:
+                ts = time.perf_counter()
                 got = backend._execute(b)
+                dt_ = time.perf_counter() - ts
+                if all(it.num_new_tokens == 1 for it in b):
+                    t_dec += dt_
+                    n_dec += 1
+                else:
+                    t_mix += dt_
                 if want is not None:
                     mismatches += sum(got[k] != v for k, v in want.items())
         elapsed = time.perf_counter() - t0
@@ -714,7 +727,7 @@ def run_engine(args: argparse.Namespace, local: int) -> None:
         "unit": "tokens/s",
         "n_gpus": 1,
         "steps": len(steps) * replays,
-        "warmup": 20,
+        "warmup": len(steps),
         "ms_per_step": round(1000 * elapsed / (len(steps) * replays), 3),
         "higher_is_better": True,
         "scaling": "weak",
@@ -726,6 +739,11 @@ def run_engine(args: argparse.Namespace, local: int) -> None:
                    "computed_tokens": n_tokens, "pool_blocks": trace["num_blocks"],
                    "prefix_hit_tokens": trace.get("prefix_hit_tokens")},
         "all_tokens_per_s": round(n_tokens * replays / elapsed, 1),
+        "decode_graphs": len(backend._graphs.graphs) if backend._graphs is not None else 0,
+        "decode_only_steps": {"count": n_dec, "avg_ms": round(1000 * t_dec / max(n_dec, 1), 3)},
+        "steps_with_prefill": {"count": len(steps) * replays - n_dec,
+                               "avg_ms": round(1000 * t_mix / max(len(steps) * replays - n_dec, 1), 3)},
+        "warmup_replay_s": round(warm_s, 2),
         "greedy_mismatches_vs_reference": mismatches if steps[0][1] is not None else None,
         "clocks": clocks.summary(),
     }  # fmt: skip

@@ -26,7 +26,7 @@ import torch
 
 from tokenserve_b200 import ops
 from tokenserve_b200.interface import Backend, BatchItem, KVCorruptionError
-from tokenserve_b200.model import PagedLlamaRunner
+from tokenserve_b200.model import DecodeGraphs, PagedLlamaRunner
 from tokenserve_b200.step import plan_step
 
 
@@ -42,6 +42,8 @@ class CudaPagedBackendConfig:
     #: Keep a device shadow of the token id in every KV slot and check each sequence's whole
     #: context every step, like SimulatedBackend(verify_kv=True) (simulated.py:86-92, 147-169).
     verify_kv: bool = False
+    #: Replay decode-only steps as captured CUDA graphs (one per batch / table-width bucket).
+    cuda_graphs: bool = True
 
     def __post_init__(self) -> None:
         if self.block_size <= 0 or self.num_blocks <= 0:
@@ -94,6 +96,7 @@ class CudaPagedBackend(Backend):
                 if config.verify_kv else None
             )  # fmt: skip
             self.runner.tag_pool = self._tags
+        self._graphs = DecodeGraphs(self.runner) if config.cuda_graphs and not config.verify_kv else None
         self.num_steps = 0
         self.num_tokens = 0
 
@@ -119,13 +122,21 @@ class CudaPagedBackend(Backend):
         cfg = self.config
         plan = plan_step(batch, cfg.block_size, cfg.num_blocks)
         with torch.cuda.device(self.device), torch.inference_mode():
-            st = self.runner.upload(plan)
-            logits = self.runner.forward(st)
+            if self._graphs is not None and plan.num_prefill == 0:
+                logits_all, greedy_all = self._graphs.run(plan)  # every decode row
+                rows = torch.from_numpy(plan.sample_rows).to(logits_all.device)
+                logits, greedy_d = logits_all[rows], greedy_all[rows]
+            else:
+                st = self.runner.upload(plan)
+                logits = self.runner.forward(st)
+                greedy_d = None
             if self._tags is not None:
                 self._verify_tags(batch)
             sampled: dict[int, int] = {}
             if logits.shape[0]:
-                greedy = torch.argmax(logits, dim=-1).cpu().numpy()
+                if greedy_d is None:
+                    greedy_d = torch.argmax(logits, dim=-1)
+                greedy = greedy_d.cpu().numpy()
                 for r, item in enumerate(plan.sample_items):
                     if item.temperature <= 0.0:
                         sampled[item.seq_id] = int(greedy[r])

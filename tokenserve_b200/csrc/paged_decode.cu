@@ -636,7 +636,14 @@ int launch_fast(const DecodeArgs& a, const CUtensorMap& km, const CUtensorMap& v
                 cudaStream_t s) {
   using G = Geometry<D>;
   auto kern = paged_decode_kernel<T, D, NT>;
-  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, G::kSmemBytes);
+  // Once per device: later calls may be captured into a CUDA graph.
+  static bool attr_done[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64 || !attr_done[dev]) {
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, G::kSmemBytes);
+    if (dev >= 0 && dev < 64) attr_done[dev] = true;
+  }
   decode_prep_kernel<T><<<1, 1024, 0, s>>>(a, a.num_q_heads * D);
   kern<<<num_sms(), kWarps * 32, G::kSmemBytes, s>>>(km, vm, a);
   return ts::launch_status("paged_decode");

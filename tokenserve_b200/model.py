@@ -177,3 +177,105 @@ class PagedLlamaRunner:
             h = h + layer.mlp(layer.post_attention_layernorm(h))
         hs = self.base.norm(h[st.sample_rows])
         return self.model.lm_head(hs).float()
+
+
+def _bucket(n: int, step: int) -> int:
+    return max(step, (n + step - 1) // step * step)
+
+
+def _pow2_bucket(n: int, floor: int = 16) -> int:
+    b = floor
+    while b < n:
+        b *= 2
+    return b
+
+
+class DecodeGraphs:
+    """CUDA graphs of whole decode steps (every sequence computes one token).
+
+    A decode step is ~35 kernel launches per layer; replaying them as one captured graph removes
+    the per-launch host cost that dominates small batches. Graphs are keyed by a batch bucket
+    (multiple of 8) and a block-table-width bucket (power of two); a step is padded to its
+    bucket with rows whose slot is -1 (K1 skips them) and whose context is 0 (K2 writes zeros),
+    so padding never touches the KV pool. Each graph owns its static input buffers and its
+    decode workspace; the KV pool and weights are the runner's own, whose addresses never change.
+    """
+
+    def __init__(self, runner: PagedLlamaRunner) -> None:
+        self.runner = runner
+        self.graphs: dict[tuple[int, int], dict] = {}
+        self.host = torch.empty(0, dtype=torch.uint8).pin_memory()
+
+    def _capture(self, b: int, w: int) -> dict:
+        r = self.runner
+        dev = r.device
+        g: dict = {"b": b, "w": w}
+        g["meta"] = torch.zeros(b * (3 * 8 + 4 + 8) + b * w * 4, dtype=torch.uint8, device=dev)
+        ids, pos, slots, dctx, dtab = self._views(g["meta"], b, w)
+        slots.fill_(-1)
+        st = DeviceStep(
+            input_ids=ids, positions=pos, slot_mapping=slots, decode_tables=dtab, decode_ctx=dctx,
+            prefill_tables=torch.zeros((0, 1), dtype=torch.int32, device=dev),
+            prefill_qsl=torch.zeros(1, dtype=torch.int32, device=dev),
+            prefill_ctx=torch.zeros(0, dtype=torch.int32, device=dev),
+            sample_rows=torch.arange(b, dtype=torch.int64, device=dev),
+            tags=torch.zeros(0, dtype=torch.int32, device=dev),
+            num_decode=b, num_prefill=0, max_query_len=0,
+        )  # fmt: skip
+        n = ops.decode_workspace_size(b, r.num_q_heads, r.num_kv_heads, r.head_dim, w,
+                                      r.block_size, r.dtype)  # fmt: skip
+        g["ws"] = torch.empty(max(n, 256), dtype=torch.uint8, device=dev)
+        saved = r._ws
+        r._ws = g["ws"]
+        try:
+            side = torch.cuda.Stream(device=dev)
+            side.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(side):
+                r.forward(st)  # warm-up outside the capture (kernel attributes, cuBLAS plans)
+            torch.cuda.current_stream().wait_stream(side)
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                logits = r.forward(st)
+                tokens = torch.argmax(logits, dim=-1)
+        finally:
+            r._ws = saved
+        g.update(graph=graph, logits=logits, tokens=tokens, st=st)
+        return g
+
+    @staticmethod
+    def _views(meta: torch.Tensor, b: int, w: int):  # type: ignore[no-untyped-def]
+        o = 0
+        ids = meta[o : o + 8 * b].view(torch.int64); o += 8 * b
+        pos = meta[o : o + 8 * b].view(torch.int64); o += 8 * b
+        slots = meta[o : o + 8 * b].view(torch.int64); o += 8 * b
+        dctx = meta[o : o + 4 * b].view(torch.int32); o += 4 * b
+        o = (o + 7) // 8 * 8
+        dtab = meta[o : o + 4 * b * w].view(torch.int32).view(b, w)
+        return ids, pos, slots, dctx, dtab
+
+    def run(self, plan: StepPlan) -> tuple[torch.Tensor, torch.Tensor]:
+        """Replays the bucket's graph for a decode-only plan; returns (logits, greedy tokens)."""
+        nb = plan.num_decode
+        b = _bucket(nb, 8)
+        w = _pow2_bucket(plan.decode_tables.shape[1])
+        g = self.graphs.get((b, w))
+        if g is None:
+            g = self.graphs[(b, w)] = self._capture(b, w)
+        size = g["meta"].numel()
+        if self.host.numel() < size:
+            self.host = torch.empty(2 * size, dtype=torch.uint8).pin_memory()
+        hv = self.host[:size]
+        ids, pos, slots, dctx, dtab = self._views(hv, b, w)
+        ids[:nb] = torch.from_numpy(plan.input_ids)
+        ids[nb:] = 0
+        pos[:nb] = torch.from_numpy(plan.positions)
+        pos[nb:] = 0
+        slots[:nb] = torch.from_numpy(plan.slot_mapping)
+        slots[nb:] = -1
+        dctx[:nb] = torch.from_numpy(plan.decode_ctx)
+        dctx[nb:] = 0
+        dtab.zero_()
+        dtab[:nb, : plan.decode_tables.shape[1]] = torch.from_numpy(plan.decode_tables)
+        g["meta"].copy_(hv, non_blocking=True)
+        g["graph"].replay()
+        return g["logits"][:nb], g["tokens"][:nb]
