@@ -281,17 +281,24 @@ __global__ void __maxnreg__(kMaxRegs)
       ts::tc::fence_after_sync();
       const int limit = pos - j * kKvTile;  // columns c <= limit are visible
       const bool full_tile = limit >= kKvTile - 1;
-      // Pass 1: row max, 32 columns at a time.
-      float mx = -INFINITY;
+      // One TMEM round trip for the whole row: four 32-column loads, one wait.
+      uint32_t sr[128];
 #pragma unroll
       for (int c4 = 0; c4 < 4; ++c4) {
-        uint32_t rr[32];
-        ts::tc::tmem_ld32(lane_base + s_col + c4 * 32, rr);
-        ts::tc::wait_ld();
+        uint32_t (&chunk)[32] = *reinterpret_cast<uint32_t(*)[32]>(sr + 32 * c4);
+        ts::tc::tmem_ld32(lane_base + s_col + c4 * 32, chunk);
+      }
+      ts::tc::wait_ld();
+      float mx = -INFINITY;
+      if (full_tile) {
 #pragma unroll
-        for (int c = 0; c < 32; ++c) {
-          const float v = __uint_as_float(rr[c]);
-          mx = fmaxf(mx, full_tile || c4 * 32 + c <= limit ? v : -INFINITY);
+        for (int c = 0; c < 128; ++c) mx = fmaxf(mx, __uint_as_float(sr[c]));
+      } else {
+#pragma unroll
+        for (int c = 0; c < 128; ++c) {
+          const float v = c <= limit ? __uint_as_float(sr[c]) : -INFINITY;
+          sr[c] = __float_as_uint(v);
+          mx = fmaxf(mx, v);
         }
       }
       // Lazy rescaling: a stale max is kept while the new one stays within 2^8 of it.
@@ -301,28 +308,20 @@ __global__ void __maxnreg__(kMaxRegs)
         corr = ex2(m_run - m_tile);
         m_run = m_tile;
       }
-      // Pass 2: P = exp2(s * scale - m), written back over the columns already read.
+      // P = exp2(s * scale - m) packed to half precision pairs in place, written over S.
       float sum0 = 0.f, sum1 = 0.f;
 #pragma unroll
-      for (int c4 = 0; c4 < 4; ++c4) {
-        uint32_t rr[32];
-        ts::tc::tmem_ld32(lane_base + s_col + c4 * 32, rr);
-        ts::tc::wait_ld();
-        uint32_t pk[16];
+      for (int c = 0; c < 128; c += 2) {
+        const float p0 = ex2(fmaf(__uint_as_float(sr[c]), sl, -m_run));
+        const float p1 = ex2(fmaf(__uint_as_float(sr[c + 1]), sl, -m_run));
+        sum0 += p0;
+        sum1 += p1;
+        sr[c / 2] = Mma::pack(p0, p1);
+      }
 #pragma unroll
-        for (int c = 0; c < 32; c += 2) {
-          const int col = c4 * 32 + c;
-          float p0 = ex2(fmaf(__uint_as_float(rr[c]), sl, -m_run));
-          float p1 = ex2(fmaf(__uint_as_float(rr[c + 1]), sl, -m_run));
-          if (!full_tile) {
-            p0 = col <= limit ? p0 : 0.f;
-            p1 = col + 1 <= limit ? p1 : 0.f;
-          }
-          sum0 += p0;
-          sum1 += p1;
-          pk[c / 2] = Mma::pack(p0, p1);
-        }
-        ts::tc::tmem_st16(lane_base + s_col + c4 * 16, pk);
+      for (int c2 = 0; c2 < 2; ++c2) {
+        uint32_t (&chunk)[32] = *reinterpret_cast<uint32_t(*)[32]>(sr + 32 * c2);
+        ts::tc::tmem_st32(lane_base + s_col + c2 * 32, chunk);
       }
       ts::tc::wait_st();
       l_run = l_run * corr + (sum0 + sum1);
