@@ -12,7 +12,8 @@
 //     both tiles of the pair share every K/V tile they need.
 //   * warp 8 (producer): Q tiles by one 3-D TMA box per 64-column half, then K/V tiles of 128
 //     tokens (8 blocks, gathered through the block table with 2-D TMA boxes, 128-byte swizzle,
-//     no multicast) into a 2-stage ring.
+//     no multicast) into a 3-stage K ring and a 2-stage V ring: a K stage is released after the
+//     last QK that reads it, a V stage after the last PV, so K loads run further ahead.
 //   * warp 9 (one lane): tcgen05.mma S_x = Q_x K^T (M=N=K=128, both K-major) into tile x's TMEM
 //     S, then O_x += P_x V with P read from TMEM (bf16, written over S) and V MN-major, in the
 //     order PV_A(j), QK_A(j+1), PV_B(j), QK_B(j+1): one tile's softmax overlaps the other's MMAs.
@@ -44,7 +45,9 @@ constexpr int kBlock = 16;                   // tokens per KV block
 constexpr int kHalfBytes = 128 * 128;        // 128 rows x 128 bytes (64 columns)
 constexpr int kTileBytes = 2 * kHalfBytes;   // 128 x 128 16-bit elements
 constexpr int kQTiles = 2;                   // query tiles per CTA (ping-pong)
-constexpr int kSmemBytes = (kQTiles + 4) * kTileBytes + 256 + 1024;
+constexpr int kKStages = 3;                  // K ring (freed after the last QK of a tile)
+constexpr int kVStages = 2;                  // V ring (freed after the last PV of a tile)
+constexpr int kSmemBytes = (kQTiles + kKStages + kVStages) * kTileBytes + 256 + 1024;
 // Warps 0..4*kQTiles-1: softmax, one warpgroup per query tile; then the producer and the MMA
 // warp. With 10 warps one SM sub-partition hosts 3 of them, so a thread may use at most
 // 16384 / 96 = 170 registers: the kernel is capped at 168.
@@ -68,7 +71,7 @@ struct PrefillArgs {
 };
 
 struct Bars {
-  uint64_t q_full, k_full[2], v_full[2], kv_empty[2];
+  uint64_t q_full, k_full[kKStages], k_empty[kKStages], v_full[kVStages], v_empty[kVStages];
   uint64_t s_full[kQTiles], p_full[kQTiles], pv_done[kQTiles];
   uint32_t tmem;
   int abort;
@@ -127,18 +130,21 @@ __global__ void __maxnreg__(kMaxRegs)
   const uint32_t raw = ts::smem_u32(smem_raw);
   uint8_t* smem = smem_raw + (((raw + 1023) & ~1023u) - raw);
   auto sQ = [&](int x) { return smem + x * kTileBytes; };
-  auto sK = [&](int st) { return smem + (kQTiles + 2 * st) * kTileBytes; };
-  auto sV = [&](int st) { return smem + (kQTiles + 2 * st + 1) * kTileBytes; };
-  Bars* bars = reinterpret_cast<Bars*>(smem + (kQTiles + 4) * kTileBytes);
+  auto sK = [&](int st) { return smem + (kQTiles + st) * kTileBytes; };
+  auto sV = [&](int st) { return smem + (kQTiles + kKStages + st) * kTileBytes; };
+  Bars* bars = reinterpret_cast<Bars*>(smem + (kQTiles + kKStages + kVStages) * kTileBytes);
   volatile int* abort = &bars->abort;
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   if (threadIdx.x == 0) {
     ts::mbar_init(&bars->q_full, 1);
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < kKStages; ++i) {
       ts::mbar_init(&bars->k_full[i], 1);
+      ts::mbar_init(&bars->k_empty[i], 1);
+    }
+    for (int i = 0; i < kVStages; ++i) {
       ts::mbar_init(&bars->v_full[i], 1);
-      ts::mbar_init(&bars->kv_empty[i], 1);
+      ts::mbar_init(&bars->v_empty[i], 1);
     }
     for (int x = 0; x < kQTiles; ++x) {
       ts::mbar_init(&bars->s_full[x], 1);
@@ -169,37 +175,47 @@ __global__ void __maxnreg__(kMaxRegs)
           ts::tc::tma_load_3d(sQ(x) + hf * kHalfBytes, &qmap, &bars->q_full, hf * 64, h * G,
                               q0 + (tile0 + x) * a.tq);
     }
-    int issued = 0;
-    for (int j = 0; j < n_max; ++j) {
-      const int st = j & 1;
-      if (j >= 2 && !wait_bar(&bars->kv_empty[st], ((j - 2) >> 1) & 1, abort)) break;
+    // K tile j goes out as soon as its stage is free (after the last QK of tile j - kKStages);
+    // V tile j one step later (its first use, PV, comes after the softmax of tile j).
+    auto load = [&](bool is_k, int j) -> bool {
+      const int nst = is_k ? kKStages : kVStages;
+      const int st = j % nst;
+      uint64_t* full = is_k ? &bars->k_full[st] : &bars->v_full[st];
+      uint64_t* empty = is_k ? &bars->k_empty[st] : &bars->v_empty[st];
+      if (j >= nst && !wait_bar(empty, ((j - nst) / nst) & 1, abort)) return false;
       const int blk0 = j * (kKvTile / kBlock);
       const int nb = min(kKvTile / kBlock, total_blk - blk0);
       const int phys_l = lane < nb ? __ldg(table + blk0 + lane) : 0;
-      if (lane == 0) {
-        ts::mbar_arrive_expect_tx(&bars->k_full[st], nb * 2 * 2048);
-        ts::mbar_arrive_expect_tx(&bars->v_full[st], nb * 2 * 2048);
-      }
+      if (lane == 0) ts::mbar_arrive_expect_tx(full, nb * 2 * 2048);
+      uint8_t* dst = is_k ? sK(st) : sV(st);
+      const void* map = is_k ? static_cast<const void*>(&kmap) : static_cast<const void*>(&vmap);
       for (int b = 0; b < kKvTile / kBlock; ++b) {
         const int phys = __shfl_sync(0xffffffffu, phys_l, b);
         if (lane == 0 && b < nb) {
           const int row = (phys * a.num_kv_heads + h) * kBlock;
-          for (int hf = 0; hf < 2; ++hf) {
-            ts::tma_load_2d(sK(st) + hf * kHalfBytes + b * 2048, &kmap, &bars->k_full[st],
-                            hf * 64, row);
-            ts::tma_load_2d(sV(st) + hf * kHalfBytes + b * 2048, &vmap, &bars->v_full[st],
-                            hf * 64, row);
-          }
+          for (int hf = 0; hf < 2; ++hf)
+            ts::tma_load_2d(dst + hf * kHalfBytes + b * 2048, map, full, hf * 64, row);
         }
       }
-      issued = j + 1;
+      return true;
+    };
+    int issued_k = 0, issued_v = 0;
+    for (int j = 0; j <= n_max; ++j) {
+      if (j < n_max) {
+        if (!load(true, j)) break;
+        issued_k = j + 1;
+      }
+      if (j >= 1) {
+        if (!load(false, j - 1)) break;
+        issued_v = j;
+      }
     }
     if (*abort && lane == 0) {
       // Let the copies still in flight land before shared memory is released.
-      for (int j = max(0, issued - 2); j < issued; ++j) {
-        ts::mbar_wait_bounded(&bars->k_full[j & 1], (j >> 1) & 1);
-        ts::mbar_wait_bounded(&bars->v_full[j & 1], (j >> 1) & 1);
-      }
+      for (int j = max(0, issued_k - kKStages); j < issued_k; ++j)
+        ts::mbar_wait_bounded(&bars->k_full[j % kKStages], (j / kKStages) & 1);
+      for (int j = max(0, issued_v - kVStages); j < issued_v; ++j)
+        ts::mbar_wait_bounded(&bars->v_full[j % kVStages], (j / kVStages) & 1);
       ts::mbar_wait_bounded(&bars->q_full, 0);
     }
   } else if (warp == mma_warp) {
@@ -211,9 +227,11 @@ __global__ void __maxnreg__(kMaxRegs)
       constexpr uint32_t idesc_pv = ts::tc::idesc_f16(BF16, kRows, 128, true);
       int last_pv[kQTiles];
       for (int x = 0; x < kQTiles; ++x) last_pv[x] = -1;
+      // The last query tile to use KV tile j releases its K (after QK) and V (after PV).
+      auto last_user = [&](int j) { return j < n_t[kQTiles - 1] ? kQTiles - 1 : 0; };
       auto issue_qk = [&](int x, int j) -> bool {
-        const int st = j & 1;
-        if (!wait_bar(&bars->k_full[st], (j >> 1) & 1, abort)) return false;
+        const int st = j % kKStages;
+        if (!wait_bar(&bars->k_full[st], (j / kKStages) & 1, abort)) return false;
         ts::tc::fence_after_sync();
         const uint32_t q_addr = ts::smem_u32(sQ(x)), k_addr = ts::smem_u32(sK(st));
 #pragma unroll
@@ -223,17 +241,18 @@ __global__ void __maxnreg__(kMaxRegs)
                          ts::tc::smem_desc_sw128(k_addr + off, 16, 1024), idesc_qk, kk > 0);
         }
         ts::tc::commit(&bars->s_full[x]);
+        if (x == last_user(j) && j + kKStages < n_max) ts::tc::commit(&bars->k_empty[st]);
         return true;
       };
       bool ok = wait_bar(&bars->q_full, 0, abort);
       for (int x = 0; ok && x < kQTiles; ++x)
         if (n_t[x] > 0) ok = issue_qk(x, 0);
       for (int j = 0; ok && j < n_max; ++j) {
-        const int st = j & 1;
+        const int st = j % kVStages;
         for (int x = 0; ok && x < kQTiles; ++x) {
           if (j >= n_t[x]) continue;
           if (!wait_bar(&bars->p_full[x], j & 1, abort) ||
-              !wait_bar(&bars->v_full[st], (j >> 1) & 1, abort)) {
+              !wait_bar(&bars->v_full[st], (j / kVStages) & 1, abort)) {
             ok = false;
             break;
           }
@@ -245,10 +264,10 @@ __global__ void __maxnreg__(kMaxRegs)
                            ts::tc::smem_desc_sw128(v_addr + kk * 2048, kHalfBytes, 1024),
                            idesc_pv, j > 0 || kk > 0);
           ts::tc::commit(&bars->pv_done[x]);
+          if (x == last_user(j) && j + kVStages < n_max) ts::tc::commit(&bars->v_empty[st]);
           last_pv[x] = j;
           if (j + 1 < n_t[x] && !issue_qk(x, j + 1)) ok = false;
         }
-        if (ok && j + 2 < n_max) ts::tc::commit(&bars->kv_empty[st]);
       }
       if (*abort)
         for (int x = 0; x < kQTiles; ++x)
@@ -273,7 +292,6 @@ __global__ void __maxnreg__(kMaxRegs)
     float m_run = -INFINITY, l_run = 0.f;
     bool ok = n_x > 0;
     for (int j = 0; ok && j < n_x; ++j) {
-      const int st = j & 1;
       if (!wait_bar(&bars->s_full[x], j & 1, abort)) {
         ok = false;
         break;
@@ -347,13 +365,14 @@ __global__ void __maxnreg__(kMaxRegs)
       if (x == zero_tile && j == n_max - 1 && j * kKvTile + kKvTile > n_kv_max) {
         // Rows past the last visible key hold stale or unwritten data: zero them so that
         // P = 0 times V stays 0.
-        if (!wait_bar(&bars->v_full[st], (j >> 1) & 1, abort)) {
+        const int vst = j % kVStages;
+        if (!wait_bar(&bars->v_full[vst], (j / kVStages) & 1, abort)) {
           ok = false;
           break;
         }
         if (j * kKvTile + r >= n_kv_max) {
-          uint4* v0 = reinterpret_cast<uint4*>(sV(st) + r * 128);
-          uint4* v1 = reinterpret_cast<uint4*>(sV(st) + kHalfBytes + r * 128);
+          uint4* v0 = reinterpret_cast<uint4*>(sV(vst) + r * 128);
+          uint4* v1 = reinterpret_cast<uint4*>(sV(vst) + kHalfBytes + r * 128);
 #pragma unroll
           for (int c = 0; c < 8; ++c) v0[c] = v1[c] = make_uint4(0, 0, 0, 0);
         }
