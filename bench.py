@@ -47,7 +47,8 @@ def parse() -> argparse.Namespace:
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["cuda", "reference"], default="cuda")
     ap.add_argument("--workload",
-                    choices=["decode", "prefill", "decode70b", "engine-tiny", "engine-8b"],
+                    choices=["decode", "prefill", "decode70b", "engine-tiny", "engine-8b",
+                             "kv-ops"],
                     default="decode",
                     help="decode: the headline decode-op line; prefill: chunked prefill with a "
                          "1024-token cached prefix, 32 layers")  # fmt: skip
@@ -259,6 +260,10 @@ def main() -> None:
     if args.workload.startswith("engine"):
         if rank == 0:
             run_engine(args, local)
+        return
+    if args.workload == "kv-ops":
+        if rank == 0:
+            run_kv_ops(args, local)
         return
     if args.impl == "reference":
         if rank == 0:
@@ -664,6 +669,77 @@ def run_decode70b(args: argparse.Namespace, world: int, rank: int, local: int) -
     if world > 1:
         dist.barrier(device_ids=[local])
         dist.destroy_process_group()
+
+
+KVOPS_METRIC = "KV scatter (K1) and block copy (K4) GB/s"
+
+
+def run_kv_ops(args: argparse.Namespace, local: int) -> None:
+    """K1 and K4 at Llama-3-8B KV geometry (8 KV heads, D=128, bf16, block 16).
+
+    K1: one 32,768-token prefill chunk (K and V rows, 128 MiB in, 128 MiB out) scattered through
+    a seeded slot mapping into a 65,536-block pool. K4: 4,096 (source, destination) block pairs
+    copied in every plane of a 32-layer [layer][K|V] pool of 8,192 blocks (64 planes, 8 GiB
+    moved). Bytes counted are read + written.
+    """
+    import torch
+
+    from tokenserve_b200 import ops
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    ops.load_library()
+    rng = np.random.default_rng(0)
+    dt = torch.bfloat16
+    g = torch.Generator(device=dev).manual_seed(5)
+    # K1
+    nb, t = 65536, 32768
+    kp = torch.zeros((nb, 8, 16, 128), dtype=dt, device=dev)
+    vp = torch.zeros_like(kp)
+    k = (torch.randn(t, 8, 128, generator=g, device=dev) * 0.5).to(dt)
+    v = (torch.randn(t, 8, 128, generator=g, device=dev) * 0.5).to(dt)
+    slots = torch.from_numpy(rng.choice(nb * 16, size=t, replace=False).astype(np.int64)).to(dev)
+    k1_bytes = 2 * (k.numel() + v.numel()) * 2 + t * 8
+    # K4
+    planes = torch.empty((64, 8192, 8, 16, 128), dtype=dt, device=dev)
+    for i in range(64):
+        planes[i].normal_(0.0, 0.5, generator=g)
+    perm = rng.permutation(8192)
+    pairs = torch.from_numpy(np.stack([perm[:4096], perm[4096:]], 1).astype(np.int64)).to(dev)
+    k4_bytes = 2 * 64 * 4096 * planes[0, 0].numel() * 2 + pairs.numel() * 8
+
+    def timed(fn, n):  # type: ignore[no-untyped-def]
+        for _ in range(max(args.warmup, 3)):
+            fn()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(n):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / 1e3 / n
+
+    with ClockSampler(dev) as clocks:
+        t1 = timed(lambda: ops.reshape_and_cache(k, v, kp, vp, slots), args.steps)
+        t4 = timed(lambda: ops.copy_blocks(planes, pairs), max(2, args.steps // 4))
+    peak, kind = peaks()
+    print(json.dumps({
+        "metric": KVOPS_METRIC,
+        "value": round(k4_bytes / t4 / 1e9, 1),
+        "unit": "GB/s",
+        "n_gpus": 1, "steps": args.steps, "warmup": max(args.warmup, 3),
+        "higher_is_better": True, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": "K1 32k-token chunk scatter; K4 4096 pairs x 64 planes"},
+        "k1_reshape_and_cache": {"bytes": k1_bytes, "us": round(t1 * 1e6, 2),
+                                 "gbs": round(k1_bytes / t1 / 1e9, 1),
+                                 "frac": round(k1_bytes / t1 / 1e9 / peak, 4)},
+        "k4_copy_blocks": {"bytes": k4_bytes, "us": round(t4 * 1e6, 2),
+                           "gbs": round(k4_bytes / t4 / 1e9, 1),
+                           "frac": round(k4_bytes / t4 / 1e9 / peak, 4)},
+        "peak": peak, "peak_kind": kind,
+        "clocks": clocks.summary(),
+    }), flush=True)  # fmt: skip
 
 
 ENGINE_METRIC = "engine decode tokens/s (recorded tokenserve engine schedule replayed)"
