@@ -7,7 +7,7 @@
 // instead of a private contiguous cache.
 //
 // Design (HBM-bound: every K/V byte is read exactly once):
-//   * Work item = (sequence b, partition p of kPartBlocks blocks, KV head h). All G = Hq/Hkv
+//   * Work item = (sequence b, partition p of pb blocks, KV head h). All G = Hq/Hkv
 //     query heads of h are packed into the N dimension of the tensor-core tiles, so a KV byte
 //     serves every query head that uses it (GQA packing).
 //   * Every warp is an independent pipeline: it claims items from a global counter, and its
@@ -31,7 +31,10 @@ namespace {
 #define TS_DECODE_WARPS 8  // independent warp pipelines per CTA (one CTA per SM)
 #endif
 #ifndef TS_DECODE_PART_BLOCKS
-#define TS_DECODE_PART_BLOCKS 64  // blocks per work item
+#define TS_DECODE_PART_BLOCKS 64  // largest work item, in blocks
+#endif
+#ifndef TS_DECODE_MIN_PART_BLOCKS
+#define TS_DECODE_MIN_PART_BLOCKS 16  // smallest work item, in blocks
 #endif
 #ifndef TS_DECODE_STAGES_D128
 #define TS_DECODE_STAGES_D128 3  // ring stages per warp at head_dim 128
@@ -45,8 +48,13 @@ namespace {
 
 constexpr int kWarps = TS_DECODE_WARPS;
 constexpr int kBlock = 16;                          // tokens per KV block
-constexpr int kPartBlocks = TS_DECODE_PART_BLOCKS;  // blocks per work item
+// Work items are pb blocks long, pb chosen per call by the prep kernel between these bounds:
+// the largest that still gives every warp of the grid at least two items (small batches get
+// short items so all warps stream, large ones long items so per-item costs stay small).
+constexpr int kPartBlocks = TS_DECODE_PART_BLOCKS;
+constexpr int kMinPartBlocks = TS_DECODE_MIN_PART_BLOCKS;
 static_assert(kPartBlocks >= 2 && kPartBlocks <= 64, "a work item's table fits two registers per lane");
+static_assert(kMinPartBlocks >= 2 && kMinPartBlocks <= kPartBlocks, "bad partition bounds");
 constexpr float kLog2e = 1.4426950408889634f;
 
 struct DecodeArgs {
@@ -62,7 +70,8 @@ struct DecodeArgs {
   int group;  // query heads per KV head
   int64_t num_blocks;
   float scale_log2;
-  int* header;  // [0] work counter, [1] status
+  int* header;  // [0] work counter, [1] status, [2] blocks per work item this call
+  int grid_warps;  // warps of the main kernel's grid
   int* prefix;  // [batch + 1] partitions before sequence b
   int4* part_info;  // [partition, in claim order] = (sequence, partition, slot partition, nparts)
   int* part_ctx;     // [partition, in claim order] = context length of its sequence
@@ -81,7 +90,7 @@ inline size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 WsLayout ws_layout(int batch, int hkv, int hd, int max_blocks, int nt) {
   WsLayout w;
   const size_t max_parts =
-      size_t(batch) * size_t((max_blocks + kPartBlocks - 1) / kPartBlocks);
+      size_t(batch) * size_t((max_blocks + kMinPartBlocks - 1) / kMinPartBlocks);
   const size_t slots = max_parts * size_t(hkv);
   w.prefix = 256;
   w.part_info = w.prefix + align256(sizeof(int) * (size_t(batch) + 1));
@@ -136,17 +145,33 @@ template <typename T>
 __global__ void __launch_bounds__(1024) decode_prep_kernel(DecodeArgs a, int row_elems) {
   __shared__ int warp_sums[32];
   __shared__ int hist[kPartBlocks], cursor[kPartBlocks];
+  __shared__ int chosen;
   const int B = a.batch;
   const int per = (B + blockDim.x - 1) / blockDim.x;
   const int b0 = threadIdx.x * per;
   if (threadIdx.x < kPartBlocks) hist[threadIdx.x] = 0;
+  // Items each candidate size would give; keep the largest size with >= 2 items per warp.
+  if (threadIdx.x == 0) chosen = kMinPartBlocks;
+  for (int cand = kPartBlocks; cand > kMinPartBlocks; cand /= 2) {
+    int n = 0;
+    for (int i = 0; i < per; ++i)
+      if (b0 + i < B) n += (clamped_blocks(a, b0 + i) + cand - 1) / cand;
+    int total = 0;
+    block_exclusive_scan(n, &total, warp_sums);
+    if (int64_t(total) * a.num_kv_heads >= 2 * int64_t(a.grid_warps)) {
+      if (threadIdx.x == 0) chosen = cand;
+      break;
+    }
+  }
+  __syncthreads();
+  const int pbk = chosen;
   int parts = 0, full = 0;
   for (int i = 0; i < per; ++i) {
     const int b = b0 + i;
     if (b < B) {
       const int nblk = clamped_blocks(a, b);
-      parts += (nblk + kPartBlocks - 1) / kPartBlocks;
-      full += nblk / kPartBlocks;
+      parts += (nblk + pbk - 1) / pbk;
+      full += nblk / pbk;
     }
   }
   __syncthreads();
@@ -159,14 +184,14 @@ __global__ void __launch_bounds__(1024) decode_prep_kernel(DecodeArgs a, int row
     if (b < B) {
       const int nblk = clamped_blocks(a, b);
       const int ctx = min(max(a.context_lens[b], 0), cap);
-      const int np = (nblk + kPartBlocks - 1) / kPartBlocks, nf = nblk / kPartBlocks;
+      const int np = (nblk + pbk - 1) / pbk, nf = nblk / pbk;
       a.prefix[b] = run_p;
       for (int p = 0; p < nf; ++p) {
         const int idx = TS_DECODE_LPT ? run_f + p : run_p + p;
         a.part_info[idx] = make_int4(b, p, run_p + p, np);
         a.part_ctx[idx] = ctx;
       }
-      if (nblk % kPartBlocks) atomicAdd(&hist[nblk % kPartBlocks], 1);
+      if (nblk % pbk) atomicAdd(&hist[nblk % pbk], 1);
       if (nblk == 0) {
         T* o = static_cast<T*>(a.out) + int64_t(b) * row_elems;
         for (int e = 0; e < row_elems; ++e) o[e] = ts::from_float<T>(0.f);
@@ -179,21 +204,22 @@ __global__ void __launch_bounds__(1024) decode_prep_kernel(DecodeArgs a, int row
   if (threadIdx.x == 0) {
     a.prefix[B] = total_parts;
     int off = total_full;
-    for (int sz = kPartBlocks - 1; sz >= 1; --sz) {  // longest partial partitions first
+    for (int sz = pbk - 1; sz >= 1; --sz) {  // longest partial partitions first
       cursor[sz] = off;
       off += hist[sz];
     }
     a.header[0] = 0;
     a.header[1] = 0;
+    a.header[2] = pbk;
   }
   __syncthreads();
   for (int i = 0; i < per; ++i) {
     const int b = b0 + i;
     if (b < B) {
       const int nblk = clamped_blocks(a, b);
-      const int r = nblk % kPartBlocks;
+      const int r = nblk % pbk;
       if (r) {
-        const int nf = nblk / kPartBlocks, pb = a.prefix[b];
+        const int nf = nblk / pbk, pb = a.prefix[b];
         const int idx = TS_DECODE_LPT ? atomicAdd(&cursor[r], 1) : pb + nf;
         a.part_info[idx] = make_int4(b, nf, pb + nf, nf + 1);
         a.part_ctx[idx] = min(max(a.context_lens[b], 0), cap);
@@ -242,7 +268,7 @@ struct ItemInfo {
 };
 
 // Work item (claim order) -> (sequence, partition, KV head): one descriptor load.
-__device__ __forceinline__ ItemInfo decode_item(const DecodeArgs& a, int item) {
+__device__ __forceinline__ ItemInfo decode_item(const DecodeArgs& a, int item, int pb) {
   ItemInfo it;
   const int pidx = item / a.num_kv_heads;
   it.h = item - pidx * a.num_kv_heads;
@@ -252,8 +278,8 @@ __device__ __forceinline__ ItemInfo decode_item(const DecodeArgs& a, int item) {
   it.part_global = pi.z;
   it.nparts = pi.w;
   it.ctx = __ldg(a.part_ctx + pidx);
-  const int rem = (it.ctx + kBlock - 1) / kBlock - it.part * kPartBlocks;
-  it.nblk = rem < kPartBlocks ? rem : kPartBlocks;
+  const int rem = (it.ctx + kBlock - 1) / kBlock - it.part * pb;
+  it.nblk = rem < pb ? rem : pb;
   return it;
 }
 
@@ -287,6 +313,7 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
   __syncwarp();
 
   const int total_items = __ldg(a.prefix + a.batch) * a.num_kv_heads;
+  const int pb = __ldg(a.header + 2);  // blocks per work item, chosen by the prep kernel
   int* counter = a.header;
 
   // ---- producer state (warp-uniform except p_table, one table entry per lane)
@@ -303,11 +330,11 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
       const int item = __shfl_sync(0xffffffffu, nxt, 0);
       if (item < total_items) {
         if (lane == 0) nxt = atomicAdd(counter, 1);
-        p_it = decode_item(a, item);
+        p_it = decode_item(a, item, pb);
         p_item = item;
         p_nblk = p_it.nblk;
         p_blk = 0;
-        const int32_t* row = a.block_tables + int64_t(p_it.b) * a.max_blocks + p_it.part * kPartBlocks;
+        const int32_t* row = a.block_tables + int64_t(p_it.b) * a.max_blocks + p_it.part * pb;
 #pragma unroll
         for (int w = 0; w < TABW; ++w)
           p_table[w] = lane + 32 * w < p_it.nblk ? __ldg(row + lane + 32 * w) : 0;
@@ -495,7 +522,7 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
     if ((md.y & 0x40000000) == 0) {
       const uint32_t kb = ts::smem_u32(ring + s * G::kStageBytes);
       const uint32_t vb = kb + G::kTileBytes;
-      const int tok0 = (it.part * kPartBlocks + md.y) * kBlock;
+      const int tok0 = (it.part * pb + md.y) * kBlock;
       const int nvalid = it.ctx - tok0;
 
       // S^T[token][head] = K Q^T
@@ -742,6 +769,7 @@ extern "C" int ts_paged_decode(void* out, const void* query, int64_t query_token
   a.group = group;
   a.num_blocks = num_blocks;
   a.scale_log2 = scale * kLog2e;
+  a.grid_warps = num_sms() * kWarps;
   a.header = reinterpret_cast<int*>(ws);
   a.prefix = reinterpret_cast<int*>(ws + w.prefix);
   a.part_info = reinterpret_cast<int4*>(ws + w.part_info);
@@ -868,6 +896,7 @@ extern "C" int ts_paged_decode_no_alloc(void* out, const void* query, int64_t qu
   a.group = group;
   a.num_blocks = num_blocks;
   a.scale_log2 = scale * kLog2e;
+  a.grid_warps = num_sms() * kWarps;
   a.header = reinterpret_cast<int*>(ws);
   a.prefix = reinterpret_cast<int*>(ws + w.prefix);
   a.part_info = reinterpret_cast<int4*>(ws + w.part_info);
