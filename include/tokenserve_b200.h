@@ -200,6 +200,39 @@ int ts_verify_tags(const int32_t* tag_pool, const int32_t* block_tables,
                    int32_t batch, int32_t block_size, int64_t num_blocks,
                    int32_t* mismatch_pos, void* stream);
 
+/*
+ * Fused element-wise parts of a Llama decoder layer used by the paged model runner. They
+ * replace transformers 5.5.0 modules (models/llama/modeling_llama.py) that tokenserve's
+ * HFBackend runs per sequence (src/tokenserve/backends/hf.py:71), with the same rounding points.
+ *
+ * ts_add_rmsnorm: residual[r] += x[r] in dtype (x may be NULL: no add), then
+ *   out[r] = weight * dtype(residual[r] * rsqrt(mean(residual[r]^2) + eps))   (LlamaRMSNorm :53-70)
+ *   out, residual, x: [num_rows][hidden]; weight: [hidden]; all of `dtype`.
+ */
+int ts_add_rmsnorm(void* out, void* residual, const void* x, const void* weight,
+                   int64_t num_rows, int32_t hidden, float eps, int32_t dtype, void* stream);
+
+/*
+ * ts_rope_and_cache: for each token t of a fused projection qkv[t] = [q heads | k heads | v heads]
+ * (head_dim each, rows qkv_token_stride elements apart): rotary embedding of q and k at
+ * positions[t] (apply_rotary_pos_emb :146-168, cos/sin of positions[t] * inv_freq[i] in fp32
+ * rounded to dtype), rotated q to q_out [num_tokens][num_q_heads][head_dim], rotated k and v
+ * written to the pool slot slot_mapping[t] exactly like ts_reshape_and_cache (slot < 0 skipped,
+ * slot past the pool skipped and flagged). inv_freq: fp32 [head_dim / 2].
+ */
+int ts_rope_and_cache(const void* qkv, int64_t qkv_token_stride, void* q_out, void* key_pool,
+                      void* value_pool, const int64_t* slot_mapping, const int64_t* positions,
+                      const float* inv_freq, int64_t num_tokens, int32_t num_q_heads,
+                      int32_t num_kv_heads, int32_t head_dim, int32_t block_size,
+                      int64_t num_blocks, int32_t dtype, int32_t* error_flag, void* stream);
+
+/*
+ * ts_silu_mul: out[r][c] = dtype(dtype(silu(gate_up[r][c])) * gate_up[r][intermediate + c])
+ * (LlamaMLP act_fn(gate) * up, :184); gate_up: [num_rows][2 * intermediate].
+ */
+int ts_silu_mul(void* out, const void* gate_up, int64_t num_rows, int32_t intermediate,
+                int32_t dtype, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -113,6 +113,37 @@ class PagedLlamaRunner:
         self.rotary = self.base.rotary_emb
         #: int32 [num_blocks * block_size] token id per slot, or None (shadow-KV check off)
         self.tag_pool: torch.Tensor | None = None
+        self.fused = self._fuse_weights()
+
+    def _fuse_weights(self) -> bool:
+        """Concatenates Q/K/V and gate/up weights so each is one GEMM; the modules' parameters
+        become views of the fused tensors (no extra memory). Returns False (module path) for
+        models this fused path does not cover: biases, non-default RoPE, non-SiLU MLPs."""
+        cfg = self.model.config
+        rope_type = (getattr(cfg, "rope_parameters", None) or {}).get("rope_type", "default")
+        if (getattr(cfg, "attention_bias", False) or getattr(cfg, "mlp_bias", False)
+                or rope_type != "default" or getattr(cfg, "hidden_act", "silu") != "silu"
+                or getattr(self.rotary, "attention_scaling", 1.0) != 1.0):  # fmt: skip
+            return False
+        self._w_qkv, self._w_gu = [], []
+        with torch.no_grad():
+            for layer in self.base.layers:
+                at, mlp = layer.self_attn, layer.mlp
+                w = torch.cat([at.q_proj.weight, at.k_proj.weight, at.v_proj.weight]).contiguous()
+                a, b = at.q_proj.weight.shape[0], at.k_proj.weight.shape[0]
+                at.q_proj.weight.data = w[:a]
+                at.k_proj.weight.data = w[a : a + b]
+                at.v_proj.weight.data = w[a + b :]
+                self._w_qkv.append(w)
+                g = torch.cat([mlp.gate_proj.weight, mlp.up_proj.weight]).contiguous()
+                i = mlp.gate_proj.weight.shape[0]
+                mlp.gate_proj.weight.data = g[:i]
+                mlp.up_proj.weight.data = g[i:]
+                self._w_gu.append(g)
+        self._inv_freq = self.rotary.inv_freq.float().contiguous()
+        self._eps = [(l.input_layernorm.variance_epsilon, l.post_attention_layernorm.variance_epsilon)
+                     for l in self.base.layers]  # fmt: skip
+        return True
 
     def workspace(self, batch: int, max_blocks: int) -> torch.Tensor | None:
         n = ops.decode_workspace_size(
@@ -147,6 +178,11 @@ class PagedLlamaRunner:
             k, v, kp, vp, st.slot_mapping,
             token_tags=st.tags if tagged else None, tag_pool=self.tag_pool if tagged else None,
         )  # fmt: skip
+        return self.attend(layer, q, st)
+
+    def attend(self, layer: int, q: torch.Tensor, st: DeviceStep) -> torch.Tensor:
+        """K2 on the decode rows and K3 on the prefill rows (the step's K/V already in the pool)."""
+        kp, vp = self.kv[layer, 0], self.kv[layer, 1]
         out = torch.empty(q.shape, dtype=q.dtype, device=q.device)
         nd = st.num_decode
         if nd:
@@ -161,6 +197,42 @@ class PagedLlamaRunner:
     @torch.inference_mode()
     def forward(self, st: DeviceStep) -> torch.Tensor:
         """Runs every layer over the step's tokens; returns float32 logits of the sampled rows."""
+        if self.fused and self.tag_pool is None:
+            return self._forward_fused(st)
+        return self._forward_modules(st)
+
+    def _forward_fused(self, st: DeviceStep) -> torch.Tensor:
+        """Per layer: add+RMSNorm, QKV GEMM, RoPE+K1, K2/K3, O GEMM, add+RMSNorm, gate-up GEMM,
+        SiLU*up, down GEMM — the same math as the modules, in ~10 kernels."""
+        f = torch.nn.functional
+        res = self.base.embed_tokens(st.input_ids)
+        t = res.shape[0]
+        hq, hkv, d = self.num_q_heads, self.num_kv_heads, self.head_dim
+        layers = self.base.layers
+        x = torch.empty_like(res)
+        ops.add_rmsnorm(x, res, None, layers[0].input_layernorm.weight, self._eps[0][0])
+        for li, layer in enumerate(layers):
+            at, mlp = layer.self_attn, layer.mlp
+            qkv = f.linear(x, self._w_qkv[li])
+            q = torch.empty((t, hq, d), dtype=res.dtype, device=res.device)
+            ops.rope_and_cache(qkv, q, self.kv[li, 0], self.kv[li, 1], st.slot_mapping,
+                               st.positions, self._inv_freq, hq, hkv)  # fmt: skip
+            o = self.attend(li, q, st)
+            a = at.o_proj(o.view(t, hq * d))
+            x2 = torch.empty_like(res)
+            ops.add_rmsnorm(x2, res, a, layer.post_attention_layernorm.weight, self._eps[li][1])
+            gu = f.linear(x2, self._w_gu[li])
+            m = torch.empty((t, gu.shape[1] // 2), dtype=res.dtype, device=res.device)
+            ops.silu_mul(m, gu)
+            mo = mlp.down_proj(m)
+            if li + 1 < len(layers):
+                ops.add_rmsnorm(x, res, mo, layers[li + 1].input_layernorm.weight,
+                                self._eps[li + 1][0])  # fmt: skip
+            else:
+                ops.add_rmsnorm(x, res, mo, self.base.norm.weight, self.base.norm.variance_epsilon)
+        return self.model.lm_head(x[st.sample_rows]).float()
+
+    def _forward_modules(self, st: DeviceStep) -> torch.Tensor:
         h = self.base.embed_tokens(st.input_ids)
         cos, sin = self.rotary(h, st.positions[None, :])
         cos, sin = cos[0], sin[0]

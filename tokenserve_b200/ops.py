@@ -45,6 +45,12 @@ _SIGNATURES: dict[str, tuple[object, list[object]]] = {
     ),
     "ts_copy_blocks": (ctypes.c_int, [_p, _i64, _i64, _i64, _i64, _p, _i64, _p, _p]),
     "ts_verify_tags": (ctypes.c_int, [_p, _p, _i32, _p, _p, _p, _i32, _i32, _i64, _p, _p]),
+    "ts_add_rmsnorm": (ctypes.c_int, [_p, _p, _p, _p, _i64, _i32, _f32, _i32, _p]),
+    "ts_rope_and_cache": (
+        ctypes.c_int,
+        [_p, _i64, _p, _p, _p, _p, _p, _p, _i64, _i32, _i32, _i32, _i32, _i64, _i32, _p, _p],
+    ),
+    "ts_silu_mul": (ctypes.c_int, [_p, _p, _i64, _i32, _i32, _p]),
 }
 
 _lib: ctypes.CDLL | None = None
@@ -251,3 +257,43 @@ def verify_tags(
         num_blocks, _ptr(mismatch_pos), _stream(),
     )  # fmt: skip
     _check(code, "verify_tags")
+
+
+def add_rmsnorm(out: torch.Tensor, residual: torch.Tensor, x: torch.Tensor | None,
+                weight: torch.Tensor, eps: float) -> None:  # fmt: skip
+    """``residual += x`` (skipped when ``x`` is None), then ``out = RMSNorm(residual) * weight``."""
+    rows, hidden = residual.shape
+    for t in (out, residual, weight) + (() if x is None else (x,)):
+        if not t.is_contiguous() or t.dtype != residual.dtype:
+            raise KernelError("add_rmsnorm: tensors must be contiguous and of one dtype")
+    code = load_library().ts_add_rmsnorm(_ptr(out), _ptr(residual), _ptr(x), _ptr(weight), rows,
+                                         hidden, float(eps), _dtype(residual), _stream())  # fmt: skip
+    _check(code, "add_rmsnorm")
+
+
+def rope_and_cache(qkv: torch.Tensor, q_out: torch.Tensor, key_pool: torch.Tensor,
+                   value_pool: torch.Tensor, slot_mapping: torch.Tensor, positions: torch.Tensor,
+                   inv_freq: torch.Tensor, num_q_heads: int, num_kv_heads: int,
+                   error_flag: torch.Tensor | None = None) -> None:  # fmt: skip
+    """RoPE on q and k of fused ``qkv [T, (Hq + 2 Hkv) * D]``; q -> ``q_out``, k/v -> the pool."""
+    nb, hkv, bs, d = _pool_dims(key_pool)
+    if hkv != num_kv_heads or qkv.stride(1) != 1 or not q_out.is_contiguous():
+        raise KernelError("rope_and_cache: bad layout")
+    if slot_mapping.dtype != torch.int64 or positions.dtype != torch.int64:
+        raise KernelError("rope_and_cache: slot_mapping and positions must be int64")
+    code = load_library().ts_rope_and_cache(
+        _ptr(qkv), qkv.stride(0), _ptr(q_out), _ptr(key_pool), _ptr(value_pool),
+        _ptr(slot_mapping), _ptr(positions), _ptr(inv_freq), qkv.shape[0], num_q_heads,
+        num_kv_heads, d, bs, nb, _dtype(key_pool), _ptr(error_flag), _stream(),
+    )  # fmt: skip
+    _check(code, "rope_and_cache")
+
+
+def silu_mul(out: torch.Tensor, gate_up: torch.Tensor) -> None:
+    """``out = silu(gate) * up`` for ``gate_up = [gate | up]`` of shape ``[T, 2 I]``."""
+    rows, two_i = gate_up.shape
+    if not gate_up.is_contiguous() or not out.is_contiguous() or out.shape != (rows, two_i // 2):
+        raise KernelError("silu_mul: bad layout")
+    code = load_library().ts_silu_mul(_ptr(out), _ptr(gate_up), rows, two_i // 2,
+                                      _dtype(gate_up), _stream())  # fmt: skip
+    _check(code, "silu_mul")
