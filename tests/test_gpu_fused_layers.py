@@ -39,7 +39,7 @@ def assert_within_ulp(got: torch.Tensor, want: torch.Tensor, min_exact: float = 
 
 
 @pytest.mark.parametrize("dtype", DTYPES)
-@pytest.mark.parametrize("hidden", [4096, 1000])
+@pytest.mark.parametrize("hidden", [4096, 1000, 1001])  # 1001: the scalar (unvectorised) kernel
 def test_add_rmsnorm_matches_llama_rmsnorm(cuda_device, dtype, hidden) -> None:  # type: ignore[no-untyped-def]
     g = torch.Generator(device=cuda_device).manual_seed(hidden)
     rows = 37
@@ -67,14 +67,17 @@ def test_add_rmsnorm_matches_llama_rmsnorm(cuda_device, dtype, hidden) -> None: 
 
 
 @pytest.mark.parametrize("dtype", DTYPES)
-def test_rope_and_cache_matches_apply_rotary_pos_emb(cuda_device, dtype) -> None:  # type: ignore[no-untyped-def]
+@pytest.mark.parametrize("padded", [False, True])  # True: odd row stride, the scalar kernel
+def test_rope_and_cache_matches_apply_rotary_pos_emb(cuda_device, dtype, padded) -> None:  # type: ignore[no-untyped-def]
     hq, hkv, d, bs, nb = 8, 2, 128, 16, 64
     t = 45
     cfg = hf.LlamaConfig(hidden_size=hq * d, num_attention_heads=hq, num_key_value_heads=hkv,
                          head_dim=d, rope_theta=500000.0)  # fmt: skip
     rot = hf.LlamaRotaryEmbedding(cfg).to(cuda_device)
     g = torch.Generator(device=cuda_device).manual_seed(3)
-    qkv = torch.randn(t, (hq + 2 * hkv) * d, generator=g, device=cuda_device).to(dtype)
+    width = (hq + 2 * hkv) * d
+    qkv = torch.randn(t, width + int(padded), generator=g, device=cuda_device).to(dtype)
+    qkv = qkv[:, :width]  # row stride width + 1 when padded
     positions = torch.randint(0, 8192, (t,), generator=g, device=cuda_device)
     slots = torch.randperm(nb * bs, generator=g, device=cuda_device)[:t].contiguous()
     slots[5] = -1  # padding row: nothing written
@@ -121,9 +124,10 @@ def test_rope_and_cache_flags_out_of_range_slot(cuda_device) -> None:  # type: i
 
 
 @pytest.mark.parametrize("dtype", DTYPES)
-def test_silu_mul_matches_llama_mlp_activation(cuda_device, dtype) -> None:  # type: ignore[no-untyped-def]
+@pytest.mark.parametrize("inter", [14336, 1001])  # 1001: the scalar kernel
+def test_silu_mul_matches_llama_mlp_activation(cuda_device, dtype, inter) -> None:  # type: ignore[no-untyped-def]
     g = torch.Generator(device=cuda_device).manual_seed(7)
-    rows, inter = 19, 14336
+    rows = 19
     gu = (3 * torch.randn(rows, 2 * inter, generator=g, device=cuda_device)).to(dtype)
     out = torch.empty(rows, inter, dtype=dtype, device=cuda_device)
     ops.silu_mul(out, gu)

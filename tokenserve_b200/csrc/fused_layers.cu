@@ -59,6 +59,78 @@ __global__ void __launch_bounds__(THREADS) add_rmsnorm_kernel(T* __restrict__ ou
   }
 }
 
+// 16-byte vector of T: one LDG.128 / STG.128.
+template <typename T>
+struct alignas(16) Vec {
+  static constexpr int E = 16 / sizeof(T);
+  T v[E];
+};
+
+// Same arithmetic as add_rmsnorm_kernel, with 16-byte accesses and the row held in registers
+// between the statistics pass and the output pass (one read of the residual instead of two).
+// Requires hidden % E == 0, hidden <= THREADS * NV * E and 16-byte aligned rows.
+template <typename T, int THREADS, int NV>
+__global__ void __launch_bounds__(THREADS) add_rmsnorm_vec_kernel(T* __restrict__ out,
+                                                                  T* __restrict__ residual,
+                                                                  const T* __restrict__ x,
+                                                                  const T* __restrict__ weight,
+                                                                  int hidden, float eps) {
+  constexpr int E = Vec<T>::E;
+  const int nvec = hidden / E;
+  const int64_t row = blockIdx.x;
+  Vec<T>* res = reinterpret_cast<Vec<T>*>(residual + row * hidden);
+  const Vec<T>* xr = x == nullptr ? nullptr : reinterpret_cast<const Vec<T>*>(x + row * hidden);
+  float v[NV][E];
+  float ss = 0.f;
+#pragma unroll
+  for (int k = 0; k < NV; ++k) {
+    const int idx = threadIdx.x + k * THREADS;
+    if (idx < nvec) {
+      Vec<T> r = res[idx];
+      if (xr != nullptr) {
+        const Vec<T> a = xr[idx];
+#pragma unroll
+        for (int e = 0; e < E; ++e) r.v[e] = rnd<T>(ts::to_float(r.v[e]) + ts::to_float(a.v[e]));
+        res[idx] = r;
+      }
+#pragma unroll
+      for (int e = 0; e < E; ++e) {
+        v[k][e] = ts::to_float(r.v[e]);
+        ss += v[k][e] * v[k][e];
+      }
+    }
+  }
+  __shared__ float red[THREADS / 32];
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  if (threadIdx.x % 32 == 0) red[threadIdx.x / 32] = ss;
+  __syncthreads();
+  float tot = 0.f;
+#pragma unroll
+  for (int w = 0; w < THREADS / 32; ++w) tot += red[w];
+  const float inv = rsqrtf(tot / float(hidden) + eps);
+  const Vec<T>* wv = reinterpret_cast<const Vec<T>*>(weight);
+  Vec<T>* o = reinterpret_cast<Vec<T>*>(out + row * hidden);
+#pragma unroll
+  for (int k = 0; k < NV; ++k) {
+    const int idx = threadIdx.x + k * THREADS;
+    if (idx < nvec) {
+      const Vec<T> w = wv[idx];
+      Vec<T> y;
+#pragma unroll
+      for (int e = 0; e < E; ++e) {
+        const T normed = rnd<T>(v[k][e] * inv);  // .to(input_dtype)
+        y.v[e] = rnd<T>(ts::to_float(w.v[e]) * ts::to_float(normed));
+      }
+      o[idx] = y;
+    }
+  }
+}
+
+__host__ __forceinline__ bool aligned16(const void* p) {
+  return (reinterpret_cast<uintptr_t>(p) & 15u) == 0;
+}
+
 // ------------------------------------------------------------------------- RoPE + K1
 
 // One CTA per token; one thread per (head, dim pair i in [0, D/2)).
@@ -111,6 +183,59 @@ __global__ void rope_and_cache_kernel(const T* __restrict__ qkv, int64_t qkv_str
   }
 }
 
+// rope_and_cache_kernel with each thread on E consecutive dimension pairs (16-byte accesses).
+// Requires (head_dim / 2) % E == 0 and 16-byte aligned rows.
+template <typename T>
+__global__ void rope_and_cache_vec_kernel(const T* __restrict__ qkv, int64_t qkv_stride,
+                                          T* __restrict__ q_out, T* __restrict__ key_pool,
+                                          T* __restrict__ value_pool,
+                                          const int64_t* __restrict__ slots,
+                                          const int64_t* __restrict__ positions,
+                                          const float* __restrict__ inv_freq, int hq, int hkv,
+                                          int d, int block_size, int64_t num_slots,
+                                          int32_t* __restrict__ error_flag) {
+  constexpr int E = Vec<T>::E;
+  const int64_t t = blockIdx.x;
+  const T* row = qkv + t * qkv_stride;
+  const float pos = float(__ldg(positions + t));
+  const int half = d / 2, cpr = half / E;
+  const int64_t slot = __ldg(slots + t);
+  const bool write_kv = slot >= 0 && slot < num_slots;
+  if (slot >= num_slots && error_flag != nullptr && threadIdx.x == 0) atomicExch(error_flag, 1);
+  const int64_t blk = write_kv ? slot / block_size : 0;
+  const int64_t off = write_kv ? slot - blk * block_size : 0;
+  for (int j = threadIdx.x; j < (hq + 2 * hkv) * cpr; j += blockDim.x) {
+    const int h = j / cpr, i0 = (j - h * cpr) * E;
+    const Vec<T> a = *reinterpret_cast<const Vec<T>*>(row + h * d + i0);
+    const Vec<T> b = *reinterpret_cast<const Vec<T>*>(row + h * d + i0 + half);
+    T* dst;
+    Vec<T> y1 = a, y2 = b;
+    if (h < hq + hkv) {
+#pragma unroll
+      for (int e = 0; e < E; ++e) {
+        const float ang = pos * __ldg(inv_freq + i0 + e);
+        const float cf = ts::to_float(rnd<T>(cosf(ang))), sf = ts::to_float(rnd<T>(sinf(ang)));
+        const float x1 = ts::to_float(a.v[e]), x2 = ts::to_float(b.v[e]);
+        y1.v[e] = rnd<T>(ts::to_float(rnd<T>(__fmul_rn(x1, cf))) +
+                         ts::to_float(rnd<T>(__fmul_rn(-x2, sf))));
+        y2.v[e] = rnd<T>(ts::to_float(rnd<T>(__fmul_rn(x2, cf))) +
+                         ts::to_float(rnd<T>(__fmul_rn(x1, sf))));
+      }
+      if (h < hq) {
+        dst = q_out + (t * hq + h) * d;
+      } else {
+        if (!write_kv) continue;
+        dst = key_pool + ((blk * hkv + (h - hq)) * block_size + off) * d;
+      }
+    } else {
+      if (!write_kv) continue;
+      dst = value_pool + ((blk * hkv + (h - hq - hkv)) * block_size + off) * d;
+    }
+    *reinterpret_cast<Vec<T>*>(dst + i0) = y1;
+    *reinterpret_cast<Vec<T>*>(dst + i0 + half) = y2;
+  }
+}
+
 // ------------------------------------------------------------------------- SiLU * up
 
 template <typename T>
@@ -128,12 +253,49 @@ __global__ void silu_mul_kernel(T* __restrict__ out, const T* __restrict__ gate_
   }
 }
 
+// silu_mul_kernel on E consecutive columns per thread (16-byte accesses).
+// Requires intermediate % E == 0 and 16-byte aligned rows.
+template <typename T>
+__global__ void silu_mul_vec_kernel(T* __restrict__ out, const T* __restrict__ gate_up,
+                                    int64_t rows, int inter) {
+  constexpr int E = Vec<T>::E;
+  const int cpr = inter / E;
+  const int64_t n = rows * cpr;
+  for (int64_t e = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; e < n;
+       e += int64_t(gridDim.x) * blockDim.x) {
+    const int64_t r = e / cpr;
+    const int c = int(e - r * cpr) * E;
+    const Vec<T> g = *reinterpret_cast<const Vec<T>*>(gate_up + r * 2 * inter + c);
+    const Vec<T> u = *reinterpret_cast<const Vec<T>*>(gate_up + r * 2 * inter + inter + c);
+    Vec<T> y;
+#pragma unroll
+    for (int k = 0; k < E; ++k) {
+      const float gf = ts::to_float(g.v[k]);
+      const T a = rnd<T>(gf / (1.f + expf(-gf)));
+      y.v[k] = rnd<T>(ts::to_float(a) * ts::to_float(u.v[k]));
+    }
+    *reinterpret_cast<Vec<T>*>(out + r * inter + c) = y;
+  }
+}
+
 template <typename T>
 int launch_add_rmsnorm(void* out, void* res, const void* x, const void* w, int64_t rows,
                        int hidden, float eps, cudaStream_t s) {
-  add_rmsnorm_kernel<T, 256><<<unsigned(rows), 256, 0, s>>>(
-      static_cast<T*>(out), static_cast<T*>(res), static_cast<const T*>(x),
-      static_cast<const T*>(w), hidden, eps);
+  constexpr int E = Vec<T>::E;
+  const bool vec = hidden % E == 0 && aligned16(out) && aligned16(res) && aligned16(w) &&
+                   (x == nullptr || aligned16(x));
+  T* o = static_cast<T*>(out);
+  T* r = static_cast<T*>(res);
+  const T* xp = static_cast<const T*>(x);
+  const T* wp = static_cast<const T*>(w);
+  if (vec && hidden <= 256 * E)
+    add_rmsnorm_vec_kernel<T, 256, 1><<<unsigned(rows), 256, 0, s>>>(o, r, xp, wp, hidden, eps);
+  else if (vec && hidden <= 256 * 2 * E)
+    add_rmsnorm_vec_kernel<T, 256, 2><<<unsigned(rows), 256, 0, s>>>(o, r, xp, wp, hidden, eps);
+  else if (vec && hidden <= 256 * 4 * E)
+    add_rmsnorm_vec_kernel<T, 256, 4><<<unsigned(rows), 256, 0, s>>>(o, r, xp, wp, hidden, eps);
+  else
+    add_rmsnorm_kernel<T, 256><<<unsigned(rows), 256, 0, s>>>(o, r, xp, wp, hidden, eps);
   return ts::launch_status("add_rmsnorm");
 }
 
@@ -175,11 +337,23 @@ extern "C" int ts_rope_and_cache(const void* qkv, int64_t qkv_token_stride, void
   const int work = (num_q_heads + 2 * num_kv_heads) * head_dim / 2;
   const int threads = work >= 512 ? 512 : ((work + 31) / 32) * 32;
   const int64_t ns = num_blocks * block_size;
+  const int esz = ts::dtype_size(dtype), ev = 16 / esz;
+  const bool vec = (head_dim / 2) % ev == 0 && (qkv_token_stride * esz) % 16 == 0 &&
+                   aligned16(qkv) && aligned16(q_out) && aligned16(key_pool) &&
+                   aligned16(value_pool);
+  const int vwork = work / ev;
+  const int vthreads = vwork >= 256 ? 256 : ((vwork + 31) / 32) * 32;
 #define TS_R(T)                                                                                 \
-  rope_and_cache_kernel<T><<<unsigned(num_tokens), threads, 0, s>>>(                           \
-      static_cast<const T*>(qkv), qkv_token_stride, static_cast<T*>(q_out),                    \
-      static_cast<T*>(key_pool), static_cast<T*>(value_pool), slot_mapping, positions,         \
-      inv_freq, num_q_heads, num_kv_heads, head_dim, block_size, ns, error_flag)
+  if (vec)                                                                                      \
+    rope_and_cache_vec_kernel<T><<<unsigned(num_tokens), vthreads, 0, s>>>(                    \
+        static_cast<const T*>(qkv), qkv_token_stride, static_cast<T*>(q_out),                  \
+        static_cast<T*>(key_pool), static_cast<T*>(value_pool), slot_mapping, positions,       \
+        inv_freq, num_q_heads, num_kv_heads, head_dim, block_size, ns, error_flag);            \
+  else                                                                                          \
+    rope_and_cache_kernel<T><<<unsigned(num_tokens), threads, 0, s>>>(                         \
+        static_cast<const T*>(qkv), qkv_token_stride, static_cast<T*>(q_out),                  \
+        static_cast<T*>(key_pool), static_cast<T*>(value_pool), slot_mapping, positions,       \
+        inv_freq, num_q_heads, num_kv_heads, head_dim, block_size, ns, error_flag)
   switch (dtype) {
     case TS_FLOAT32: TS_R(float); break;
     case TS_FLOAT16: TS_R(__half); break;
@@ -198,6 +372,27 @@ extern "C" int ts_silu_mul(void* out, const void* gate_up, int64_t num_rows,
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int64_t n = num_rows * intermediate;
   const unsigned grid = unsigned(n / 256 + 1 < 148 * 16 ? n / 256 + 1 : 148 * 16);
+  const int ev = 16 / ts::dtype_size(dtype);
+  if (intermediate % ev == 0 && aligned16(out) && aligned16(gate_up)) {
+    const int64_t nv = n / ev;
+    const unsigned vgrid = unsigned(nv / 256 + 1 < 148 * 16 ? nv / 256 + 1 : 148 * 16);
+    switch (dtype) {
+      case TS_FLOAT32:
+        silu_mul_vec_kernel<float><<<vgrid, 256, 0, s>>>(
+            static_cast<float*>(out), static_cast<const float*>(gate_up), num_rows, intermediate);
+        break;
+      case TS_FLOAT16:
+        silu_mul_vec_kernel<__half><<<vgrid, 256, 0, s>>>(
+            static_cast<__half*>(out), static_cast<const __half*>(gate_up), num_rows, intermediate);
+        break;
+      default:
+        silu_mul_vec_kernel<__nv_bfloat16><<<vgrid, 256, 0, s>>>(
+            static_cast<__nv_bfloat16*>(out), static_cast<const __nv_bfloat16*>(gate_up), num_rows,
+            intermediate);
+        break;
+    }
+    return ts::launch_status("silu_mul");
+  }
   switch (dtype) {
     case TS_FLOAT32:
       silu_mul_kernel<float><<<grid, 256, 0, s>>>(static_cast<float*>(out),
