@@ -48,7 +48,7 @@ def parse() -> argparse.Namespace:
     ap.add_argument("--impl", choices=["cuda", "reference"], default="cuda")
     ap.add_argument("--workload",
                     choices=["decode", "prefill", "decode70b", "engine-tiny", "engine-8b",
-                             "kv-ops"],
+                             "kv-ops", "swap"],
                     default="decode",
                     help="decode: the headline decode-op line; prefill: chunked prefill with a "
                          "1024-token cached prefix, 32 layers")  # fmt: skip
@@ -264,6 +264,10 @@ def main() -> None:
     if args.workload == "kv-ops":
         if rank == 0:
             run_kv_ops(args, local)
+        return
+    if args.workload == "swap":
+        if rank == 0:
+            run_swap(args, local)
         return
     if args.impl == "reference":
         if rank == 0:
@@ -866,6 +870,111 @@ def run_engine(args: argparse.Namespace, local: int) -> None:
                                           "is infeasible; the tiny-Llama engine carries the "
                                           "CPU comparison"}  # fmt: skip
     print(json.dumps(line), flush=True)
+
+
+SWAP_METRIC = "swap-to-host preemption: KV swap-out + swap-in GB/s (vs recompute time)"
+
+
+def run_swap(args: argparse.Namespace, local: int) -> None:
+    """Swap-to-host preemption against recompute, for the Llama-3-8B engine model.
+
+    For a preempted sequence of C tokens (C = 512, 2048, 8192): swap-out of its ceil(C/16)
+    blocks (every layer's K and V, 2 MiB a block) into a pinned host arena and swap-in into other
+    pool blocks, through ``CudaPagedBackend.swap_out`` / ``swap_in`` (K4 across the host link),
+    against recomputing the sequence: a C-token prefill through ``CudaPagedBackend.execute`` in
+    2048-token chunks (the scheduler's default budget). The link reference is a plain pinned
+    ``cudaMemcpyAsync`` of the same bytes each way.
+    """
+    import torch
+
+    from tokenserve_b200.backend import CudaPagedBackend, CudaPagedBackendConfig
+    from tokenserve_b200.interface import BatchItem
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    ctxs = [512, 2048, 8192]
+    max_blocks = max(ctxs) // 16
+    backend = CudaPagedBackend(build_model("engine-8b", dev), CudaPagedBackendConfig(
+        block_size=16, num_blocks=2 * max_blocks + 8, device=str(dev),
+        swap_space_blocks=max_blocks))  # fmt: skip
+    backend.runner.kv.normal_(0.0, 0.5)
+    block_bytes = backend.runner.block_bytes
+    rng = np.random.default_rng(0)
+    rows = []
+
+    def ev_time(fn, n):  # type: ignore[no-untyped-def]
+        for _ in range(max(args.warmup, 3)):
+            fn()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(n):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / 1e3 / n
+
+    def wall(fn, n):  # type: ignore[no-untyped-def]
+        for _ in range(max(args.warmup, 3)):
+            fn()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        for _ in range(n):
+            fn()
+        torch.cuda.synchronize()
+        return (time.perf_counter() - t0) / n
+
+    n_rep = max(3, args.steps // 4)
+    with ClockSampler(dev) as clocks:
+        # The link's own speed: one contiguous pinned copy of the largest swap each way.
+        nbytes = max_blocks * block_bytes
+        dbuf = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+        hbuf = torch.empty(nbytes, dtype=torch.uint8).pin_memory()
+        d2h = ev_time(lambda: hbuf.copy_(dbuf, non_blocking=True), n_rep)
+        h2d = ev_time(lambda: dbuf.copy_(hbuf, non_blocking=True), n_rep)
+        del dbuf, hbuf
+        for c in ctxs:
+            n = c // 16
+            src = [int(b) for b in rng.permutation(max_blocks)[:n]]
+            dst = [max_blocks + 8 + i for i in range(n)]
+            t_out = wall(lambda: backend.swap_out([(b, i) for i, b in enumerate(src)]), n_rep)
+            t_in = wall(lambda: backend.swap_in([(i, b) for i, b in enumerate(dst)]), n_rep)
+            toks = [int(x) for x in rng.integers(0, 128256, c)]
+
+            def recompute() -> None:
+                for s0 in range(0, c, 2048):
+                    m = min(2048, c - s0)
+                    end = s0 + m
+                    backend._execute([BatchItem(1, toks, s0, m, c, list(range(-(-end // 16))),
+                                                end == c, 0)])  # fmt: skip
+
+            t_rc = wall(recompute, max(2, n_rep // 2))
+            rows.append({"context_tokens": c, "blocks": n, "bytes": n * block_bytes,
+                         "swap_out_ms": round(t_out * 1e3, 3), "swap_in_ms": round(t_in * 1e3, 3),
+                         "swap_gbs": round(2 * n * block_bytes / (t_out + t_in) / 1e9, 1),
+                         "recompute_ms": round(t_rc * 1e3, 3),
+                         "recompute_over_swap": round(t_rc / (t_out + t_in), 2)})  # fmt: skip
+    link = {"d2h_gbs": round(nbytes / d2h / 1e9, 1), "h2d_gbs": round(nbytes / h2d / 1e9, 1)}
+    big = rows[-1]
+    link_gbs = 2 * nbytes / (d2h + h2d) / 1e9
+    print(json.dumps({
+        "metric": SWAP_METRIC,
+        "value": big["swap_gbs"],
+        "unit": "GB/s",
+        "n_gpus": 1, "steps": n_rep, "warmup": max(args.warmup, 3),
+        "ms_per_step": round(big["swap_out_ms"] + big["swap_in_ms"], 3),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": "Llama-3-8B KV (32 layers, 8 kv heads, D 128, block 16, 2 MiB "
+                               "a block), preempted sequences of 512/2048/8192 tokens",
+                   "recompute": "prefill through CudaPagedBackend.execute in 2048-token chunks"},
+        "per_context": rows,
+        "roofline": {"bound": "host link", "achieved": big["swap_gbs"],
+                     "peak": round(link_gbs, 1), "peak_kind": "pinned cudaMemcpyAsync, same bytes",
+                     "unit": "GB/s", "frac": round(big["swap_gbs"] / link_gbs, 4)},
+        "link": link,
+        "clocks": clocks.summary(),
+    }), flush=True)  # fmt: skip
 
 
 PREFILL_METRIC = "chunked-prefill paged attention TFLOP/s (bf16, % of tensor peak)"

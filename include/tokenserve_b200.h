@@ -186,6 +186,28 @@ int ts_copy_blocks(void* pool_base, int64_t num_planes, int64_t plane_stride_byt
                    int64_t num_pairs, int32_t* error_flag, void* stream);
 
 /*
+ * K4 swap form — the same block copy between two arenas of one plane layout, for swap-to-host
+ * preemption: swap-out copies pool blocks into a pinned host arena, swap-in copies them back
+ * (into any free blocks). The kernel reads or writes the host side directly through its
+ * device-mapped address.
+ *
+ * Replaces: nothing in the reference (recompute-only preemption, src/tokenserve/scheduler.py:
+ * 215-225; swap-to-host is listed as future work in its README, "What a GPU run would add").
+ *
+ * dst_base / src_base: arenas of num_planes planes; block b of plane p of an arena starts at
+ *                      base + p * plane_stride_bytes + b * block_bytes. Each must be memory of
+ *                      the current device or pinned (page-locked) host memory; anything else
+ *                      (pageable host memory, another device's memory) returns
+ *                      TS_ERR_INVALID_ARGUMENT before any launch. src_dst and error_flag too.
+ * src_dst:             int64 [num_pairs][2] of (block in src arena, block in dst arena); a
+ *                      pair out of either arena's range is skipped and sets *error_flag.
+ */
+int ts_swap_blocks(void* dst_base, int64_t dst_plane_stride_bytes, int64_t dst_num_blocks,
+                   const void* src_base, int64_t src_plane_stride_bytes, int64_t src_num_blocks,
+                   int64_t num_planes, int64_t block_bytes, const int64_t* src_dst,
+                   int64_t num_pairs, int32_t* error_flag, void* stream);
+
+/*
  * Shadow-KV verification of the token tags written by ts_reshape_and_cache: for each
  * sequence, every position 0..context_lens[b]-1 read back through its block table must hold
  * expected_tokens (concatenated per sequence at expected_offsets[b]). The first mismatch per

@@ -92,6 +92,16 @@ def gather(pool: np.ndarray, block_table: Sequence[int], ctx_len: int) -> np.nda
     return np.ascontiguousarray(pool[slots // bs, :, slots % bs, :].transpose(1, 0, 2))
 
 
+def swap_blocks(dst: np.ndarray, src: np.ndarray, pairs: np.ndarray) -> None:
+    """``dst[p, d] = src[p, s]`` for every plane ``p`` and pair ``(s, d)``: a block copy between
+    two arenas of one plane layout (device pool and host swap space). Swap-to-host has no code in
+    the reference (its scheduler preempts by recompute, scheduler.py:215-225); this is the copy
+    semantics a swap-out followed by a swap-in must preserve."""
+    pairs = np.asarray(pairs, dtype=np.int64).reshape(-1, 2)
+    if pairs.size:
+        dst[:, pairs[:, 1]] = src[:, pairs[:, 0]]
+
+
 def copy_blocks(planes: np.ndarray, pairs: np.ndarray) -> None:
     """``planes[p, dst] = planes[p, src]`` for every plane ``p`` and pair ``(src, dst)``."""
     pairs = np.asarray(pairs, dtype=np.int64).reshape(-1, 2)

@@ -32,7 +32,8 @@ def test_header_declares_the_entry_points() -> None:
     names = declared()
     for want in ("ts_reshape_and_cache", "ts_paged_decode", "ts_paged_prefill",
                  "ts_copy_blocks", "ts_version", "ts_last_error", "ts_verify_tags",
-                 "ts_paged_decode_workspace_size"):  # fmt: skip
+                 "ts_paged_decode_workspace_size", "ts_swap_blocks", "ts_add_rmsnorm",
+                 "ts_rope_and_cache", "ts_silu_mul"):  # fmt: skip
         assert want in names
 
 
@@ -70,6 +71,11 @@ def test_argument_errors_are_reported_before_any_launch(lib: ctypes.CDLL) -> Non
     assert rc == -1 and b"bad sizes" in lib.ts_last_error()
     rc = lib.ts_copy_blocks(None, 2, 10, 100, 1, None, 1, None, None)
     assert rc == -1 and b"copy_blocks" in lib.ts_last_error()
+    rc = lib.ts_swap_blocks(None, 10, 100, None, 4096, 4, 2, 64, None, 1, None, None)
+    assert rc == -1 and b"swap_blocks: bad sizes" in lib.ts_last_error()
+    rc = lib.ts_swap_blocks(None, 6400, 100, None, 256, 4, 2, 64, None, 1, None, None)
+    assert rc == -1 and b"null pointer" in lib.ts_last_error()
+    assert lib.ts_swap_blocks(None, 6400, 100, None, 256, 4, 2, 64, None, 0, None, None) == 0
     # Empty work is a successful no-op and clears the message.
     assert lib.ts_paged_prefill(None, None, 4096, None, None, None, 1, None, None, 0, 0, 0, 32,
                                 8, 128, 16, 10, 0.1, ops.TS_BFLOAT16, None) == 0  # fmt: skip

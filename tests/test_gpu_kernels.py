@@ -134,6 +134,52 @@ def test_copy_blocks_bit_exact(cuda_device, dtype) -> None:  # type: ignore[no-u
     assert torch.equal(dev.cpu(), torch.from_numpy(ref).to(dtype))
 
 
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_swap_blocks_round_trip_bit_exact(cuda_device, dtype) -> None:  # type: ignore[no-untyped-def]
+    """Swap-out to pinned host memory, then swap-in to other pool blocks: both arenas match the
+    oracle's index copies bit for bit, and untouched blocks stay as they were."""
+    planes, nb, hb = 6, 40, 8
+    g = torch.Generator().manual_seed(11)
+    pool = torch.randn(planes, nb, 2, 16, 64, generator=g).to(dtype)
+    host = torch.zeros(planes, hb, 2, 16, 64, dtype=dtype).pin_memory()
+    out_pairs = np.array([[3, 0], [17, 5], [39, 7]], dtype=np.int64)  # (pool, host)
+    in_pairs = np.array([[0, 10], [5, 11], [7, 0]], dtype=np.int64)  # (host, pool)
+    ref_pool = pool.float().numpy().copy()
+    ref_host = host.float().numpy().copy()
+    okv.swap_blocks(ref_host, ref_pool, out_pairs)
+    okv.swap_blocks(ref_pool, ref_host, in_pairs)
+    dev = pool.to(cuda_device)
+    flag = torch.zeros(1, dtype=torch.int32, device=cuda_device)
+    ops.swap_blocks(host, dev, torch.from_numpy(out_pairs).to(cuda_device), flag)
+    torch.cuda.synchronize()
+    assert torch.equal(host, torch.from_numpy(ref_host).to(dtype))
+    ops.swap_blocks(dev, host, torch.from_numpy(in_pairs).to(cuda_device), flag)
+    torch.cuda.synchronize()
+    assert torch.equal(dev.cpu(), torch.from_numpy(ref_pool).to(dtype))
+    assert int(flag) == 0
+    # A pair outside either arena is skipped and flagged.
+    before = host.clone()
+    ops.swap_blocks(host, dev, torch.tensor([[1, hb]], device=cuda_device), flag)
+    torch.cuda.synchronize()
+    assert int(flag) == 1 and torch.equal(host, before)
+
+
+def test_swap_blocks_refuses_pageable_memory(cuda_device) -> None:  # type: ignore[no-untyped-def]
+    """Pageable host memory is rejected before any launch (a kernel cannot address it)."""
+    import ctypes
+
+    lib = ops.load_library()
+    dev = torch.zeros(2, 4, 64, dtype=torch.uint8, device=cuda_device)
+    pageable = np.zeros((2, 4, 64), dtype=np.uint8)
+    pairs = torch.tensor([[0, 1]], device=cuda_device)
+    rc = lib.ts_swap_blocks(ctypes.c_void_p(pageable.ctypes.data), 256, 4, ctypes.c_void_p(dev.data_ptr()),
+                            256, 4, 2, 64, ctypes.c_void_p(pairs.data_ptr()), 1, None, None)  # fmt: skip
+    assert rc == ops.TS_ERR_INVALID_ARGUMENT
+    assert b"pinned host memory" in lib.ts_last_error()
+    with pytest.raises(ops.KernelError, match="pinned"):
+        ops.swap_blocks(torch.zeros(2, 4, 64, dtype=torch.uint8), dev, pairs)
+
+
 # ------------------------------------------------------------------------------ K2
 
 DECODE_CTX = [1, 2, 15, 16, 17, 31, 255, 256, 257, 511, 700, 1024, 3000, 4100]

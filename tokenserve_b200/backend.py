@@ -18,6 +18,7 @@ the block tables again (engine.py:1-13).
 from __future__ import annotations
 
 import asyncio
+import dataclasses
 from collections.abc import Sequence as Seq
 from dataclasses import dataclass
 
@@ -44,6 +45,9 @@ class CudaPagedBackendConfig:
     verify_kv: bool = False
     #: Replay decode-only steps as captured CUDA graphs (one per batch / table-width bucket).
     cuda_graphs: bool = True
+    #: Blocks of pinned host memory for swap-to-host preemption (:meth:`CudaPagedBackend.swap_out`);
+    #: 0 = no swap space. A block holds every layer's K and V for ``block_size`` tokens.
+    swap_space_blocks: int = 0
 
     def __post_init__(self) -> None:
         if self.block_size <= 0 or self.num_blocks <= 0:
@@ -97,8 +101,79 @@ class CudaPagedBackend(Backend):
             )  # fmt: skip
             self.runner.tag_pool = self._tags
         self._graphs = DecodeGraphs(self.runner) if config.cuda_graphs and not config.verify_kv else None
+        r = self.runner
+        #: pinned host arena [layers * 2][swap blocks][block plane] (same plane layout as the pool)
+        self.swap_space = (
+            torch.empty((r.num_layers * 2, config.swap_space_blocks,
+                         r.num_kv_heads * r.block_size * r.head_dim), dtype=r.dtype,
+                        pin_memory=True)
+            if config.swap_space_blocks > 0 else None
+        )  # fmt: skip
+        self._flag = torch.zeros(1, dtype=torch.int32, device=self.device)
         self.num_steps = 0
         self.num_tokens = 0
+
+    # ------------------------------------------------------------ block copy / swap hooks
+
+    def _planes(self) -> torch.Tensor:
+        """The pool as ``[layers * 2, num_blocks, block plane]`` (a view, no copy)."""
+        kv = self.runner.kv
+        return kv.view(kv.shape[0] * 2, kv.shape[2], -1)
+
+    def _pairs(self, pairs: Seq[tuple[int, int]]) -> torch.Tensor:
+        host = torch.tensor(list(pairs), dtype=torch.int64).reshape(-1, 2)
+        return host.to(self.device, non_blocking=False)
+
+    def _finish(self, what: str) -> None:
+        flag = int(self._flag.item())  # synchronises the stream
+        if flag:
+            self._flag.zero_()
+            raise ValueError(f"{what}: a block id is outside the pool or the swap space")
+
+    def copy_blocks(self, src_dst: Seq[tuple[int, int]]) -> None:
+        """K4 over every layer's K and V: block ``dst`` becomes a copy of block ``src``
+        (copy-on-write of a shared partial block, defragmentation). Returns after the copy."""
+        if not src_dst:
+            return
+        with torch.cuda.device(self.device):
+            ops.copy_blocks(self._planes(), self._pairs(src_dst), self._flag)
+            self._finish("copy_blocks")
+
+    def swap_out(self, device_to_host: Seq[tuple[int, int]]) -> None:
+        """Swap-to-host preemption: copies pool block ``d`` into swap-space block ``h`` for each
+        pair ``(d, h)``; the pool blocks can be handed to other sequences once this returns."""
+        self._swap(device_to_host, out=True)
+
+    def swap_in(self, host_to_device: Seq[tuple[int, int]]) -> None:
+        """Resumes a swapped sequence: copies swap-space block ``h`` into pool block ``d`` for
+        each pair ``(h, d)`` (any free pool blocks; the table is rewritten with them)."""
+        self._swap(host_to_device, out=False)
+
+    def _swap(self, pairs: Seq[tuple[int, int]], *, out: bool) -> None:
+        if self.swap_space is None:
+            raise RuntimeError("no swap space: set CudaPagedBackendConfig.swap_space_blocks")
+        if not pairs:
+            return
+        with torch.cuda.device(self.device):
+            planes = self._planes()
+            dst, src = (self.swap_space, planes) if out else (planes, self.swap_space)
+            ops.swap_blocks(dst, src, self._pairs(pairs), self._flag)
+            self._finish("swap_out" if out else "swap_in")
+
+    def resize_pool(self, num_blocks: int) -> None:
+        """Re-creates the KV pool (and the shadow tags) with ``num_blocks`` blocks. Only legal
+        before the engine starts: every cached block is dropped. Captured decode graphs hold the
+        old pool's address, so they are dropped too."""
+        with torch.cuda.device(self.device):
+            self._graphs = None
+            self.runner.resize_pool(num_blocks)
+            if self._tags is not None:
+                self._tags = torch.full((num_blocks * self.config.block_size,), -1,
+                                        dtype=torch.int32, device=self.device)  # fmt: skip
+                self.runner.tag_pool = self._tags
+        self.config = dataclasses.replace(self.config, num_blocks=num_blocks)
+        if self.config.cuda_graphs and not self.config.verify_kv:
+            self._graphs = DecodeGraphs(self.runner)
 
     @property
     def max_position_embeddings(self) -> int | None:

@@ -115,6 +115,24 @@ class PagedLlamaRunner:
         self.tag_pool: torch.Tensor | None = None
         self.fused = self._fuse_weights()
 
+    @property
+    def block_bytes(self) -> int:
+        """Device bytes one KV block takes over all layers, K and V."""
+        return 2 * self.num_layers * self.num_kv_heads * self.block_size * self.head_dim * (
+            torch.finfo(self.dtype).bits // 8)  # fmt: skip
+
+    def resize_pool(self, num_blocks: int) -> None:
+        """Replaces the KV pool by a zeroed one of ``num_blocks`` blocks (the old one is freed
+        first, so peak memory is the larger of the two)."""
+        if num_blocks <= 0:
+            raise ValueError("num_blocks must be positive")
+        shape = (self.num_layers, 2, num_blocks, self.num_kv_heads, self.block_size,
+                 self.head_dim)  # fmt: skip
+        self.kv = torch.empty(0, dtype=self.dtype, device=self.device)
+        torch.cuda.empty_cache()
+        self.kv = torch.zeros(shape, dtype=self.dtype, device=self.device)
+        self.num_blocks = num_blocks
+
     def _fuse_weights(self) -> bool:
         """Concatenates Q/K/V and gate/up weights so each is one GEMM; the modules' parameters
         become views of the fused tensors (no extra memory). Returns False (module path) for

@@ -17,6 +17,7 @@ LIB_PATH = Path(__file__).resolve().parent / "_lib" / "libtokenserve_b200.so"
 ABI_VERSION = 1
 
 TS_FLOAT32, TS_FLOAT16, TS_BFLOAT16 = 0, 1, 2
+TS_ERR_INVALID_ARGUMENT, TS_ERR_UNSUPPORTED, TS_ERR_WORKSPACE, TS_ERR_MISALIGNED = -1, -2, -3, -4
 DTYPE_CODES = {torch.float32: TS_FLOAT32, torch.float16: TS_FLOAT16, torch.bfloat16: TS_BFLOAT16}
 
 _p = ctypes.c_void_p
@@ -45,6 +46,9 @@ _SIGNATURES: dict[str, tuple[object, list[object]]] = {
     ),
     "ts_copy_blocks": (ctypes.c_int, [_p, _i64, _i64, _i64, _i64, _p, _i64, _p, _p]),
     "ts_verify_tags": (ctypes.c_int, [_p, _p, _i32, _p, _p, _p, _i32, _i32, _i64, _p, _p]),
+    "ts_swap_blocks": (
+        ctypes.c_int, [_p, _i64, _i64, _p, _i64, _i64, _i64, _i64, _p, _i64, _p, _p]
+    ),
     "ts_add_rmsnorm": (ctypes.c_int, [_p, _p, _p, _p, _i64, _i32, _f32, _i32, _p]),
     "ts_rope_and_cache": (
         ctypes.c_int,
@@ -231,6 +235,8 @@ def copy_blocks(
         raise KernelError("planes must be a contiguous [P, num_blocks, ...] tensor")
     if src_dst.dtype != torch.int64 or not src_dst.is_contiguous():
         raise KernelError("src_dst must be contiguous int64 [n, 2]")
+    if not planes.is_cuda or src_dst.device != planes.device:
+        raise KernelError("planes and src_dst must be on the same CUDA device")
     es = planes.element_size()
     block_bytes = planes[0, 0].numel() * es
     code = load_library().ts_copy_blocks(
@@ -238,6 +244,29 @@ def copy_blocks(
         _ptr(src_dst), src_dst.numel() // 2, _ptr(error_flag), _stream(),
     )  # fmt: skip
     _check(code, "copy_blocks")
+
+
+def swap_blocks(dst: torch.Tensor, src: torch.Tensor, src_dst: torch.Tensor,
+                error_flag: torch.Tensor | None = None) -> None:  # fmt: skip
+    """K4 between two arenas ``[P, blocks, ...]`` of one plane layout: ``dst[p, d] = src[p, s]``
+    for each pair ``(s, d)``. One side may be pinned host memory (swap-out / swap-in)."""
+    for t in (dst, src):
+        if not t.is_contiguous() or t.dim() < 2:
+            raise KernelError("swap_blocks: arenas must be contiguous [P, blocks, ...] tensors")
+        if not t.is_cuda and not t.is_pinned():
+            raise KernelError("swap_blocks: a host arena must be pinned memory")
+    if dst.shape[0] != src.shape[0] or dst[0, 0].numel() * dst.element_size() != (
+            src[0, 0].numel() * src.element_size()):  # fmt: skip
+        raise KernelError("swap_blocks: arenas differ in planes or block size")
+    if src_dst.dtype != torch.int64 or not src_dst.is_contiguous() or not src_dst.is_cuda:
+        raise KernelError("swap_blocks: src_dst must be contiguous int64 [n, 2] on the device")
+    bb = dst[0, 0].numel() * dst.element_size()
+    code = load_library().ts_swap_blocks(
+        _ptr(dst), dst.stride(0) * dst.element_size(), dst.shape[1],
+        _ptr(src), src.stride(0) * src.element_size(), src.shape[1],
+        dst.shape[0], bb, _ptr(src_dst), src_dst.numel() // 2, _ptr(error_flag), _stream(),
+    )  # fmt: skip
+    _check(code, "swap_blocks")
 
 
 def verify_tags(
