@@ -805,6 +805,14 @@ def run_engine(args: argparse.Namespace, local: int) -> None:
     replays = max(1, args.replays)
     t_dec = t_mix = 0.0
     n_dec = 0
+    # Algorithmic HBM bytes of a decode-only step: every weight except the embedding table (only
+    # the batch's rows are gathered) once, plus each sequence's whole K/V context in every layer.
+    r = backend.runner
+    emb = r.base.embed_tokens.weight
+    weight_bytes = sum(p.numel() * p.element_size() for p in r.model.parameters()) - (
+        emb.numel() * emb.element_size())  # fmt: skip
+    kv_token_bytes = r.block_bytes // r.block_size
+    dec_bytes = 0
     with ClockSampler(dev) as clocks:
         t0 = time.perf_counter()
         for _ in range(replays):
@@ -815,6 +823,7 @@ def run_engine(args: argparse.Namespace, local: int) -> None:
                 if all(it.num_new_tokens == 1 for it in b):
                     t_dec += dt_
                     n_dec += 1
+                    dec_bytes += weight_bytes + kv_token_bytes * sum(it.end for it in b)
                 else:
                     t_mix += dt_
                 if want is not None:
@@ -846,6 +855,17 @@ def run_engine(args: argparse.Namespace, local: int) -> None:
         "greedy_mismatches_vs_reference": mismatches if steps[0][1] is not None else None,
         "clocks": clocks.summary(),
     }  # fmt: skip
+    peak, peak_kind = peaks()
+    if n_dec:
+        ach = dec_bytes / t_dec / 1e9
+        line["roofline"] = {
+            "bound": "hbm", "achieved": round(ach, 1), "peak": peak, "peak_kind": peak_kind,
+            "unit": "GB/s", "frac": round(ach / peak, 4), "traffic": None,
+            "scope": "decode-only engine steps, wall time per execute(): weights (embedding "
+                     "table excluded) + every sequence's K/V context, read once per step",
+            "weight_bytes": weight_bytes,
+            "kv_bytes_per_context_token": kv_token_bytes,
+        }  # fmt: skip
     if args.workload == "engine-tiny" and not args.no_cpu_baseline:
         from oracle.hf_engine import HFStepLoop
 
