@@ -12,8 +12,9 @@
 //     both tiles of the pair share every K/V tile they need.
 //   * warp 8 (producer): Q tiles by one 3-D TMA box per 64-column half, then K/V tiles of 128
 //     tokens (8 blocks, gathered through the block table with 2-D TMA boxes, 128-byte swizzle,
-//     no multicast) into a 3-stage K ring and a 2-stage V ring: a K stage is released after the
-//     last QK that reads it, a V stage after the last PV, so K loads run further ahead.
+//     no multicast; lane b issues block b's boxes, its table entry read one tile ahead) into a
+//     3-stage K ring and a 2-stage V ring: a K stage is released after the last QK that reads it,
+//     a V stage after the last PV, so K loads run further ahead.
 //   * warp 9 (one lane): tcgen05.mma S_x = Q_x K^T (M=N=K=128, both K-major) into tile x's TMEM
 //     S, then O_x += P_x V with P read from TMEM (bf16, written over S) and V MN-major, in the
 //     order PV_A(j), QK_A(j+1), PV_B(j), QK_B(j+1): one tile's softmax overlaps the other's MMAs.
@@ -85,6 +86,12 @@ __device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t phase, volatile
   }
   *abort = 1;
   return false;
+}
+
+__device__ __forceinline__ float max3f(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
 }
 
 __device__ __forceinline__ float ex2(float x) {
@@ -177,38 +184,47 @@ __global__ void __maxnreg__(kMaxRegs)
     }
     // K tile j goes out as soon as its stage is free (after the last QK of tile j - kKStages);
     // V tile j one step later (its first use, PV, comes after the softmax of tile j).
-    auto load = [&](bool is_k, int j) -> bool {
+    // Lane b < 8 owns block b of a KV tile: it holds that block's pool row, read from the block
+    // table one tile ahead (so the table load's latency is off the issue path), and issues the
+    // block's two TMA boxes; a tile costs one warp-wide issue instead of 16 serial ones.
+    constexpr int kBpt = kKvTile / kBlock;
+    auto table_row = [&](int j) -> int {
+      const int b = j * kBpt + lane;
+      return (lane < kBpt && j < n_max && b < total_blk)
+                 ? (__ldg(table + b) * a.num_kv_heads + h) * kBlock
+                 : -1;
+    };
+    auto load = [&](bool is_k, int j, int row) -> bool {
       const int nst = is_k ? kKStages : kVStages;
       const int st = j % nst;
       uint64_t* full = is_k ? &bars->k_full[st] : &bars->v_full[st];
       uint64_t* empty = is_k ? &bars->k_empty[st] : &bars->v_empty[st];
       if (j >= nst && !wait_bar(empty, ((j - nst) / nst) & 1, abort)) return false;
-      const int blk0 = j * (kKvTile / kBlock);
-      const int nb = min(kKvTile / kBlock, total_blk - blk0);
-      const int phys_l = lane < nb ? __ldg(table + blk0 + lane) : 0;
+      const int nb = min(kBpt, total_blk - j * kBpt);  // lanes with row >= 0
       if (lane == 0) ts::mbar_arrive_expect_tx(full, nb * 2 * 2048);
-      uint8_t* dst = is_k ? sK(st) : sV(st);
-      const void* map = is_k ? static_cast<const void*>(&kmap) : static_cast<const void*>(&vmap);
-      for (int b = 0; b < kKvTile / kBlock; ++b) {
-        const int phys = __shfl_sync(0xffffffffu, phys_l, b);
-        if (lane == 0 && b < nb) {
-          const int row = (phys * a.num_kv_heads + h) * kBlock;
-          for (int hf = 0; hf < 2; ++hf)
-            ts::tma_load_2d(dst + hf * kHalfBytes + b * 2048, map, full, hf * 64, row);
-        }
+      __syncwarp();
+      if (row >= 0) {
+        uint8_t* dst = (is_k ? sK(st) : sV(st)) + lane * 2048;
+        const void* map = is_k ? static_cast<const void*>(&kmap) : static_cast<const void*>(&vmap);
+        ts::tma_load_2d(dst, map, full, 0, row);
+        ts::tma_load_2d(dst + kHalfBytes, map, full, 64, row);
       }
       return true;
     };
     int issued_k = 0, issued_v = 0;
+    int row_k = table_row(0), row_v = -1;
     for (int j = 0; j <= n_max; ++j) {
+      const int row_next = table_row(j + 1);
       if (j < n_max) {
-        if (!load(true, j)) break;
+        if (!load(true, j, row_k)) break;
         issued_k = j + 1;
       }
       if (j >= 1) {
-        if (!load(false, j - 1)) break;
+        if (!load(false, j - 1, row_v)) break;
         issued_v = j;
       }
+      row_v = row_k;
+      row_k = row_next;
     }
     if (*abort && lane == 0) {
       // Let the copies still in flight land before shared memory is released.
@@ -229,16 +245,21 @@ __global__ void __maxnreg__(kMaxRegs)
       for (int x = 0; x < kQTiles; ++x) last_pv[x] = -1;
       // The last query tile to use KV tile j releases its K (after QK) and V (after PV).
       auto last_user = [&](int j) { return j < n_t[kQTiles - 1] ? kQTiles - 1 : 0; };
+      // Shared-memory descriptors are built once; a tile or K step only adds its byte offset
+      // / 16 to the start-address field (every address is below 256 KB, so it never carries).
+      const uint64_t dq0 = ts::tc::smem_desc_sw128(ts::smem_u32(sQ(0)), 16, 1024);
+      const uint64_t dk0 = ts::tc::smem_desc_sw128(ts::smem_u32(sK(0)), 16, 1024);
+      const uint64_t dv0 = ts::tc::smem_desc_sw128(ts::smem_u32(sV(0)), kHalfBytes, 1024);
       auto issue_qk = [&](int x, int j) -> bool {
         const int st = j % kKStages;
         if (!wait_bar(&bars->k_full[st], (j / kKStages) & 1, abort)) return false;
         ts::tc::fence_after_sync();
-        const uint32_t q_addr = ts::smem_u32(sQ(x)), k_addr = ts::smem_u32(sK(st));
+        const uint64_t dq = dq0 + uint64_t((x * kTileBytes) >> 4);
+        const uint64_t dk = dk0 + uint64_t((st * kTileBytes) >> 4);
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
-          const uint32_t off = (kk >> 2) * kHalfBytes + (kk & 3) * 32;
-          ts::tc::mma_ss(tmem + x * 128, ts::tc::smem_desc_sw128(q_addr + off, 16, 1024),
-                         ts::tc::smem_desc_sw128(k_addr + off, 16, 1024), idesc_qk, kk > 0);
+          const uint32_t off16 = ((kk >> 2) * kHalfBytes + (kk & 3) * 32) >> 4;
+          ts::tc::mma_ss(tmem + x * 128, dq + off16, dk + off16, idesc_qk, kk > 0);
         }
         ts::tc::commit(&bars->s_full[x]);
         if (x == last_user(j) && j + kKStages < n_max) ts::tc::commit(&bars->k_empty[st]);
@@ -257,12 +278,11 @@ __global__ void __maxnreg__(kMaxRegs)
             break;
           }
           ts::tc::fence_after_sync();
-          const uint32_t v_addr = ts::smem_u32(sV(st));
+          const uint64_t dv = dv0 + uint64_t((st * kTileBytes) >> 4);
 #pragma unroll
           for (int kk = 0; kk < 8; ++kk)
             ts::tc::mma_ts(tmem + 256 + x * 128, tmem + x * 128 + kk * 8,
-                           ts::tc::smem_desc_sw128(v_addr + kk * 2048, kHalfBytes, 1024),
-                           idesc_pv, j > 0 || kk > 0);
+                           dv + uint64_t((kk * 2048) >> 4), idesc_pv, j > 0 || kk > 0);
           ts::tc::commit(&bars->pv_done[x]);
           if (x == last_user(j) && j + kVStages < n_max) ts::tc::commit(&bars->v_empty[st]);
           last_pv[x] = j;
@@ -299,42 +319,65 @@ __global__ void __maxnreg__(kMaxRegs)
       ts::tc::fence_after_sync();
       const int limit = pos - j * kKvTile;  // columns c <= limit are visible
       const bool full_tile = limit >= kKvTile - 1;
-      // One TMEM round trip for the whole row: four 32-column loads, one wait.
+      // One TMEM round trip for the whole row: four 32-column loads, one wait; columns past
+      // the causal limit become -inf.
       uint32_t sr[128];
+      auto load_s = [&]() {
 #pragma unroll
-      for (int c4 = 0; c4 < 4; ++c4) {
-        uint32_t (&chunk)[32] = *reinterpret_cast<uint32_t(*)[32]>(sr + 32 * c4);
-        ts::tc::tmem_ld32(lane_base + s_col + c4 * 32, chunk);
-      }
-      ts::tc::wait_ld();
-      float mx = -INFINITY;
-      if (full_tile) {
-#pragma unroll
-        for (int c = 0; c < 128; ++c) mx = fmaxf(mx, __uint_as_float(sr[c]));
-      } else {
-#pragma unroll
-        for (int c = 0; c < 128; ++c) {
-          const float v = c <= limit ? __uint_as_float(sr[c]) : -INFINITY;
-          sr[c] = __float_as_uint(v);
-          mx = fmaxf(mx, v);
+        for (int c4 = 0; c4 < 4; ++c4) {
+          uint32_t (&chunk)[32] = *reinterpret_cast<uint32_t(*)[32]>(sr + 32 * c4);
+          ts::tc::tmem_ld32(lane_base + s_col + c4 * 32, chunk);
         }
-      }
-      // Lazy rescaling: a stale max is kept while the new one stays within 2^8 of it.
-      const float m_tile = mx * sl;
-      float corr = 1.f;
-      if (m_tile > m_run + kRescaleSlack) {
-        corr = ex2(m_run - m_tile);
-        m_run = m_tile;
-      }
-      // P = exp2(s * scale - m) packed to half precision pairs in place, written over S.
-      float sum0 = 0.f, sum1 = 0.f;
+        ts::tc::wait_ld();
+        if (!full_tile) {
 #pragma unroll
-      for (int c = 0; c < 128; c += 2) {
-        const float p0 = ex2(fmaf(__uint_as_float(sr[c]), sl, -m_run));
-        const float p1 = ex2(fmaf(__uint_as_float(sr[c + 1]), sl, -m_run));
-        sum0 += p0;
-        sum1 += p1;
-        sr[c / 2] = Mma::pack(p0, p1);
+          for (int c = 0; c < 128; ++c)
+            if (c > limit) sr[c] = __float_as_uint(-INFINITY);
+        }
+      };
+      // P = exp2(s * scale - m_run) packed to half precision pairs in place (over S), with
+      // the row sum and the largest exponent seen (xm), which the exponentials do not wait on.
+      float sum0, sum1, xm;
+      auto exp_pass = [&]() {
+        sum0 = 0.f;
+        sum1 = 0.f;
+        float xa = -INFINITY, xb = -INFINITY;
+#pragma unroll
+        for (int c = 0; c < 128; c += 4) {
+          const float x0 = fmaf(__uint_as_float(sr[c]), sl, -m_run);
+          const float x1 = fmaf(__uint_as_float(sr[c + 1]), sl, -m_run);
+          const float x2 = fmaf(__uint_as_float(sr[c + 2]), sl, -m_run);
+          const float x3 = fmaf(__uint_as_float(sr[c + 3]), sl, -m_run);
+          xa = max3f(xa, x0, x1);
+          xb = max3f(xb, x2, x3);
+          const float p0 = ex2(x0), p1 = ex2(x1), p2 = ex2(x2), p3 = ex2(x3);
+          sum0 += p0 + p2;
+          sum1 += p1 + p3;
+          sr[c / 2] = Mma::pack(p0, p1);
+          sr[c / 2 + 1] = Mma::pack(p2, p3);
+        }
+        xm = fmaxf(xa, xb);
+      };
+      load_s();
+      float corr = 1.f;
+      if (j == 0) {
+        // First tile: the exact row max (column 0 is always visible, so it is finite).
+        float mx = -INFINITY;
+#pragma unroll
+        for (int c = 0; c < 128; c += 2)
+          mx = max3f(mx, __uint_as_float(sr[c]), __uint_as_float(sr[c + 1]));
+        m_run = mx * sl;
+      }
+      exp_pass();
+      // Lazy rescaling: the running max is kept while no exponent exceeds it by more than
+      // kRescaleSlack (P <= 2^8). Rows past that take the new max and recompute the tile.
+      if (j > 0 && __any_sync(0xffffffffu, xm > kRescaleSlack)) {
+        load_s();
+        if (xm > kRescaleSlack) {
+          corr = ex2(-xm);
+          m_run += xm;
+        }
+        exp_pass();
       }
 #pragma unroll
       for (int c2 = 0; c2 < 2; ++c2) {
