@@ -28,7 +28,7 @@ import torch
 from tokenserve_b200 import ops
 from tokenserve_b200.interface import Backend, BatchItem, KVCorruptionError
 from tokenserve_b200.model import DecodeGraphs, PagedLlamaRunner
-from tokenserve_b200.step import plan_step
+from tokenserve_b200.step import plan_decode, plan_step
 
 
 @dataclass(frozen=True, slots=True)
@@ -184,7 +184,10 @@ class CudaPagedBackend(Backend):
         return await asyncio.to_thread(self._execute, list(batch))
 
     def free(self, seq_id: int) -> None:
-        """Nothing to drop: KV blocks are owned and recycled by tokenserve's KVCacheManager."""
+        """KV blocks are owned and recycled by tokenserve's KVCacheManager; only the sequence's
+        row of the device block-table mirror is released."""
+        if self._graphs is not None:
+            self._graphs.mirror.release(seq_id)
 
     async def close(self) -> None:
         self.runner.kv = torch.empty(0, device=self.device)
@@ -195,13 +198,16 @@ class CudaPagedBackend(Backend):
         if not batch:
             return {}
         cfg = self.config
-        plan = plan_step(batch, cfg.block_size, cfg.num_blocks)
+        graphs = self._graphs
+        decode_only = all(it.num_new_tokens == 1 for it in batch)
         with torch.cuda.device(self.device), torch.inference_mode():
-            if self._graphs is not None and plan.num_prefill == 0:
-                logits_all, greedy_all = self._graphs.run(plan)  # every decode row
+            if graphs is not None and decode_only and graphs.fits(batch):
+                plan = plan_decode(batch, cfg.block_size, cfg.num_blocks, graphs.mirror)
+                logits_all, greedy_all = graphs.run(plan)  # every decode row
                 rows = torch.from_numpy(plan.sample_rows).to(logits_all.device)
                 logits, greedy_d = logits_all[rows], greedy_all[rows]
             else:
+                plan = plan_step(batch, cfg.block_size, cfg.num_blocks)
                 st = self.runner.upload(plan)
                 logits = self.runner.forward(st)
                 greedy_d = None

@@ -17,7 +17,7 @@ import numpy as np
 import torch
 
 from tokenserve_b200 import ops
-from tokenserve_b200.step import StepPlan
+from tokenserve_b200.step import BlockTableMirror, DecodePlan, StepPlan
 
 
 def _rope(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.Tensor:
@@ -283,26 +283,41 @@ def _pow2_bucket(n: int, floor: int = 16) -> int:
 class DecodeGraphs:
     """CUDA graphs of whole decode steps (every sequence computes one token).
 
-    A decode step is ~35 kernel launches per layer; replaying them as one captured graph removes
-    the per-launch host cost that dominates small batches. Graphs are keyed by a batch bucket
-    (multiple of 8) and a block-table-width bucket (power of two); a step is padded to its
-    bucket with rows whose slot is -1 (K1 skips them) and whose context is 0 (K2 writes zeros),
-    so padding never touches the KV pool. Each graph owns its static input buffers and its
-    decode workspace; the KV pool and weights are the runner's own, whose addresses never change.
+    Replaying a step as one captured graph removes the per-launch host cost that dominates small
+    batches. Graphs are keyed by a batch bucket (multiple of 8) and a block-table-width bucket
+    (power of two). Block tables live in a :class:`~tokenserve_b200.step.BlockTableMirror` on
+    the device: a step uploads its new table entries (applied before the replay) and one mirror
+    row per sequence, and the graph gathers its ``[b, w]`` table from the mirror. A step is
+    padded to its bucket with rows whose slot is -1 (K1 skips them), whose context is 0 (K2
+    writes zeros) and whose mirror row is the all-zero row 0, so padding never touches the KV
+    pool. Each graph owns its static input buffers and decode workspace; the KV pool, the
+    mirror and the weights keep their addresses for the graphs' lifetime.
     """
 
-    def __init__(self, runner: PagedLlamaRunner) -> None:
+    def __init__(self, runner: PagedLlamaRunner, max_rows: int = 4096) -> None:
         self.runner = runner
         self.graphs: dict[tuple[int, int], dict] = {}
         self.host = torch.empty(0, dtype=torch.uint8).pin_memory()
+        cols = 64
+        limit = getattr(runner.model.config, "max_position_embeddings", None) or 8192
+        while cols * runner.block_size < limit:
+            cols *= 2
+        self.mirror = BlockTableMirror(max_rows, cols)
+        self.tables = torch.zeros((max_rows, cols), dtype=torch.int32, device=runner.device)
+        self._delta_host = torch.empty(0, dtype=torch.int64).pin_memory()
+        self._delta_dev = torch.empty(0, dtype=torch.int64, device=runner.device)
+
+    def fits(self, batch: list) -> bool:  # type: ignore[type-arg]
+        return self.mirror.fits(batch)
 
     def _capture(self, b: int, w: int) -> dict:
         r = self.runner
         dev = r.device
         g: dict = {"b": b, "w": w}
-        g["meta"] = torch.zeros(b * (3 * 8 + 4 + 8) + b * w * 4, dtype=torch.uint8, device=dev)
-        ids, pos, slots, dctx, dtab = self._views(g["meta"], b, w)
+        g["meta"] = torch.zeros(b * (8 * 4 + 4) + 8, dtype=torch.uint8, device=dev)
+        ids, pos, slots, dctx, rows = self._views(g["meta"], b)
         slots.fill_(-1)
+        dtab = torch.zeros((b, w), dtype=torch.int32, device=dev)
         st = DeviceStep(
             input_ids=ids, positions=pos, slot_mapping=slots, decode_tables=dtab, decode_ctx=dctx,
             prefill_tables=torch.zeros((0, 1), dtype=torch.int32, device=dev),
@@ -325,6 +340,7 @@ class DecodeGraphs:
             torch.cuda.current_stream().wait_stream(side)
             graph = torch.cuda.CUDAGraph()
             with torch.cuda.graph(graph):
+                torch.index_select(self.tables[:, :w], 0, rows, out=dtab)
                 logits = r.forward(st)
                 tokens = torch.argmax(logits, dim=-1)
         finally:
@@ -333,21 +349,33 @@ class DecodeGraphs:
         return g
 
     @staticmethod
-    def _views(meta: torch.Tensor, b: int, w: int):  # type: ignore[no-untyped-def]
+    def _views(meta: torch.Tensor, b: int):  # type: ignore[no-untyped-def]
         o = 0
         ids = meta[o : o + 8 * b].view(torch.int64); o += 8 * b
         pos = meta[o : o + 8 * b].view(torch.int64); o += 8 * b
         slots = meta[o : o + 8 * b].view(torch.int64); o += 8 * b
-        dctx = meta[o : o + 4 * b].view(torch.int32); o += 4 * b
-        o = (o + 7) // 8 * 8
-        dtab = meta[o : o + 4 * b * w].view(torch.int32).view(b, w)
-        return ids, pos, slots, dctx, dtab
+        rows = meta[o : o + 8 * b].view(torch.int64); o += 8 * b
+        dctx = meta[o : o + 4 * b].view(torch.int32)
+        return ids, pos, slots, dctx, rows
 
-    def run(self, plan: StepPlan) -> tuple[torch.Tensor, torch.Tensor]:
-        """Replays the bucket's graph for a decode-only plan; returns (logits, greedy tokens)."""
+    def _apply_deltas(self, deltas: np.ndarray) -> None:
+        n = deltas.shape[0]
+        if n == 0:
+            return
+        if self._delta_host.numel() < 3 * n:
+            self._delta_host = torch.empty(6 * n, dtype=torch.int64).pin_memory()
+            self._delta_dev = torch.empty(6 * n, dtype=torch.int64, device=self.runner.device)
+        hv = self._delta_host[: 3 * n].view(3, n)
+        hv.copy_(torch.from_numpy(np.ascontiguousarray(deltas.T)))
+        dv = self._delta_dev[: 3 * n].view(3, n)
+        dv.copy_(hv, non_blocking=True)
+        self.tables.index_put_((dv[0], dv[1]), dv[2].to(torch.int32))
+
+    def run(self, plan: DecodePlan) -> tuple[torch.Tensor, torch.Tensor]:
+        """Replays the bucket's graph for a decode plan; returns (logits, greedy tokens)."""
         nb = plan.num_decode
         b = _bucket(nb, 8)
-        w = _pow2_bucket(plan.decode_tables.shape[1])
+        w = min(_pow2_bucket(plan.width), self.mirror.max_cols)
         g = self.graphs.get((b, w))
         if g is None:
             g = self.graphs[(b, w)] = self._capture(b, w)
@@ -355,17 +383,18 @@ class DecodeGraphs:
         if self.host.numel() < size:
             self.host = torch.empty(2 * size, dtype=torch.uint8).pin_memory()
         hv = self.host[:size]
-        ids, pos, slots, dctx, dtab = self._views(hv, b, w)
+        ids, pos, slots, dctx, rows = self._views(hv, b)
         ids[:nb] = torch.from_numpy(plan.input_ids)
         ids[nb:] = 0
         pos[:nb] = torch.from_numpy(plan.positions)
         pos[nb:] = 0
         slots[:nb] = torch.from_numpy(plan.slot_mapping)
         slots[nb:] = -1
+        rows[:nb] = torch.from_numpy(plan.rows)
+        rows[nb:] = 0
         dctx[:nb] = torch.from_numpy(plan.decode_ctx)
         dctx[nb:] = 0
-        dtab.zero_()
-        dtab[:nb, : plan.decode_tables.shape[1]] = torch.from_numpy(plan.decode_tables)
+        self._apply_deltas(plan.deltas)
         g["meta"].copy_(hv, non_blocking=True)
         g["graph"].replay()
         return g["logits"][:nb], g["tokens"][:nb]

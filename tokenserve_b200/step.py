@@ -149,3 +149,151 @@ def plan_step(batch: Sequence[BatchItem], block_size: int, num_blocks: int) -> S
         sample_rows=np.asarray(sample_rows, dtype=np.int64),
         sample_items=sample_items,
     )
+
+
+# --------------------------------------------------------------------------- block-table mirror
+
+
+class BlockTableMirror:
+    """Device-resident copy of the running sequences' block tables.
+
+    tokenserve's KVCacheManager only ever appends to a running sequence's table
+    (``allocate_slots``, src/tokenserve/kv_cache.py:203-242) and frees it whole on preemption or
+    completion, after which the engine calls ``Backend.free`` (engine.py:303-304, 384). So the
+    backend keeps one device row per live sequence and, per decode step, uploads only the entries
+    appended since the last step (usually none: a new block every ``block_size`` tokens) plus one
+    row index per sequence; the step's ``[B, w]`` table is gathered on the device. A table whose
+    synced prefix changed (a preempted sequence re-admitted with other blocks) is rewritten
+    whole, and entries past a row's new length are zeroed, so a gathered table is exactly the
+    zero-padded table the host would have built. Row 0 is all zeros and serves padding rows.
+    """
+
+    def __init__(self, max_rows: int, max_cols: int) -> None:
+        if max_rows < 2 or max_cols < 1:
+            raise ValueError("a mirror needs at least one sequence row and one column")
+        self.max_rows = max_rows
+        self.max_cols = max_cols
+        self._rows: dict[int, int] = {}  # seq_id -> row
+        self._synced: dict[int, list[int]] = {}  # seq_id -> entries on the device
+        self._free = list(range(max_rows - 1, 0, -1))
+        self._row_len = [0] * max_rows  # columns of each device row that may be non-zero
+        self._last_use: dict[int, int] = {}
+        self._clock = 0
+
+    def __contains__(self, seq_id: int) -> bool:
+        return seq_id in self._rows
+
+    def release(self, seq_id: int) -> None:
+        row = self._rows.pop(seq_id, None)
+        if row is not None:
+            self._synced.pop(seq_id, None)
+            self._last_use.pop(seq_id, None)
+            self._free.append(row)
+
+    def fits(self, items: Sequence[BatchItem]) -> bool:
+        return len(items) < self.max_rows and all(len(it.block_table) <= self.max_cols
+                                                  for it in items)  # fmt: skip
+
+    def sync(self, items: Sequence[BatchItem]) -> tuple[np.ndarray, np.ndarray]:
+        """Row index per item and the ``[n, 3]`` int64 (row, column, block) entries to write."""
+        self._clock += 1
+        in_step = {it.seq_id for it in items}
+        rows = np.empty(len(items), dtype=np.int64)
+        writes: list[tuple[int, int, list[int]]] = []
+        for i, it in enumerate(items):
+            sid = it.seq_id
+            table = list(it.block_table)
+            row = self._rows.get(sid)
+            if row is None:
+                if not self._free:
+                    self._evict(in_step)
+                row = self._free.pop()
+                self._rows[sid] = row
+                self._synced[sid] = []
+            synced = self._synced[sid]
+            n = len(synced)
+            if n and len(table) >= n and table[:n] == synced:
+                if len(table) > n:
+                    writes.append((row, n, table[n:]))
+            else:
+                stale = self._row_len[row] - len(table)
+                writes.append((row, 0, table + [0] * max(0, stale)))
+            self._row_len[row] = len(table)
+            self._synced[sid] = table
+            self._last_use[sid] = self._clock
+            rows[i] = row
+        total = sum(len(v) for _, _, v in writes)
+        deltas = np.empty((total, 3), dtype=np.int64)
+        k = 0
+        for row, col, vals in writes:
+            m = len(vals)
+            deltas[k : k + m, 0] = row
+            deltas[k : k + m, 1] = np.arange(col, col + m)
+            deltas[k : k + m, 2] = vals
+            k += m
+        return rows, deltas
+
+    def _evict(self, keep: set[int]) -> None:
+        """Frees the least recently used row of a sequence outside this step."""
+        victims = [(t, s) for s, t in self._last_use.items() if s not in keep]
+        if not victims:
+            raise RuntimeError("block-table mirror full with sequences of this step")
+        self.release(min(victims)[1])
+
+
+@dataclass
+class DecodePlan:
+    """A decode-only step against a :class:`BlockTableMirror`: no table is built on the host."""
+
+    input_ids: np.ndarray  # int64 [B]
+    positions: np.ndarray  # int64 [B]
+    slot_mapping: np.ndarray  # int64 [B]
+    decode_ctx: np.ndarray  # int32 [B]
+    rows: np.ndarray  # int64 [B] mirror row of each sequence
+    deltas: np.ndarray  # int64 [n, 3] (row, column, block) entries to write first
+    width: int  # longest table of the step
+    sample_items: list[BatchItem] = field(default_factory=list)
+    sample_rows: np.ndarray = field(default_factory=lambda: np.zeros(0, dtype=np.int64))
+
+    @property
+    def num_decode(self) -> int:
+        return int(self.decode_ctx.shape[0])
+
+    @property
+    def num_prefill(self) -> int:
+        return 0
+
+    @property
+    def num_tokens(self) -> int:
+        return int(self.input_ids.shape[0])
+
+
+def plan_decode(batch: Sequence[BatchItem], block_size: int, num_blocks: int,
+                mirror: BlockTableMirror) -> DecodePlan:  # fmt: skip
+    """:func:`plan_step` for a step in which every item computes one token, with the block
+    tables kept in ``mirror``: the same checks and errors, O(batch) host work."""
+    bs = block_size
+    n = len(batch)
+    if any(it.num_new_tokens != 1 for it in batch):
+        raise ValueError("plan_decode takes decode-only steps")
+    end = np.fromiter((it.end for it in batch), dtype=np.int64, count=n)
+    tlen = np.fromiter((len(it.block_table) for it in batch), dtype=np.int64, count=n)
+    if (tlen * bs < end).any():
+        _raise_first_error(batch, bs)
+    pos = end - 1
+    blk = np.fromiter((it.block_table[p // bs] for it, p in zip(batch, pos.tolist())),
+                      dtype=np.int64, count=n)  # fmt: skip
+    slots = blk * bs + pos % bs
+    if np.unique(slots).size != n:
+        _raise_first_error(batch, bs)
+    rows, deltas = mirror.sync(batch)
+    if deltas.size and ((deltas[:, 2] < 0) | (deltas[:, 2] >= num_blocks)).any():
+        bad = int(deltas[(deltas[:, 2] < 0) | (deltas[:, 2] >= num_blocks)][0, 2])
+        for it in batch:  # the mirror must not keep an entry the device never received
+            mirror.release(it.seq_id)
+        raise ValueError(f"block id {bad} outside a pool of {num_blocks} blocks")
+    ids = np.fromiter((it.token_ids[it.end - 1] for it in batch), dtype=np.int64, count=n)
+    sample_items = [it for it in batch if it.sample]
+    sample_rows = np.fromiter((r for r, it in enumerate(batch) if it.sample), dtype=np.int64)
+    return DecodePlan(ids, pos, slots, end.astype(np.int32), rows, deltas,
+                      max(1, int(tlen.max()) if n else 1), sample_items, sample_rows)  # fmt: skip
