@@ -7,12 +7,15 @@
 // instead of a private contiguous cache.
 //
 // Design (HBM-bound: every K/V byte is read exactly once):
-//   * Work item = (sequence b, partition p of pb blocks, KV head h). All G = Hq/Hkv
-//     query heads of h are packed into the N dimension of the tensor-core tiles, so a KV byte
-//     serves every query head that uses it (GQA packing).
-//   * Every warp is an independent pipeline: it claims items from a global counter, and its
-//     lane 0 streams the item's blocks with 2-D TMA loads (128-byte swizzle, no multicast) into
-//     a private ring of kStages stages, each holding one block's K and V tile for head h.
+//   * Work item = partition of one (sequence b, KV head h): up to 64 consecutive blocks. All
+//     G = Hq/Hkv query heads of h are packed into the N dimension of the tensor-core tiles, so a
+//     KV byte serves every query head that uses it (GQA packing).
+//   * A one-CTA prep kernel splits the step's (sequence, head, block) units evenly over the
+//     grid's warps (static balance: every warp streams the same number of blocks whatever the
+//     batch) and cuts each warp's range into partitions at sequence-head ends and every 64
+//     blocks. Every warp is an independent pipeline over its own partitions: lane 0 streams
+//     their blocks with 2-D TMA loads (128-byte swizzle, no multicast) into a private ring of
+//     kStages stages, each holding one block's K and V tile for head h.
 //   * S^T = K Q^T and O^T += V^T P^T on mma.sync m16n8k16 (fp32 accumulate). P is split into a
 //     hi and a lo half-precision part so the PV product keeps ~16 mantissa bits.
 //   * Online softmax in fp32 (exp2 domain) per block; partitions of one (b, h) are merged by the
@@ -20,6 +23,7 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <algorithm>
 #include <mutex>
 
 #include "common.cuh"
@@ -33,8 +37,8 @@ namespace {
 #ifndef TS_DECODE_PART_BLOCKS
 #define TS_DECODE_PART_BLOCKS 64  // largest work item, in blocks
 #endif
-#ifndef TS_DECODE_MIN_PART_BLOCKS
-#define TS_DECODE_MIN_PART_BLOCKS 16  // smallest work item, in blocks
+#ifndef TS_DECODE_STATIC_MAX_BLOCKS
+#define TS_DECODE_STATIC_MAX_BLOCKS 80  // static split below this many blocks per warp
 #endif
 #ifndef TS_DECODE_STAGES_D128
 #define TS_DECODE_STAGES_D128 3  // ring stages per warp at head_dim 128
@@ -42,19 +46,28 @@ namespace {
 #ifndef TS_DECODE_ONE_BOX
 #define TS_DECODE_ONE_BOX 0  // 1: one 4 KiB TMA box per 128-dim tile instead of two 2 KiB
 #endif
-#ifndef TS_DECODE_LPT
-#define TS_DECODE_LPT 1  // 1: full partitions first, then partial ones by decreasing size
-#endif
 
 constexpr int kWarps = TS_DECODE_WARPS;
 constexpr int kBlock = 16;                          // tokens per KV block
-// Work items are pb blocks long, pb chosen per call by the prep kernel between these bounds:
-// the largest that still gives every warp of the grid at least two items (small batches get
-// short items so all warps stream, large ones long items so per-item costs stay small).
+// Work is split statically and evenly. The grid's warps form NG = min(G / H, WB) groups of H
+// (one warp per KV head); group g takes blocks [floor(g WB / NG), floor((g + 1) WB / NG)) of
+// the step's WB blocks (all sequences' blocks in order) and warp (g, h) attends head h over
+// them, cut into partitions of at most kPartBlocks blocks wherever a sequence or the range
+// ends. Every warp streams the same number of blocks (+-1) whatever the batch, so small
+// batches keep all warps busy to the end, and the H warps of a group (neighbours in one CTA)
+// read the H heads of the same blocks, which sit next to each other in the pool.
+//
+// Large steps instead use dynamic claiming (the split above would cut more sequences and leave
+// the partition merges unevenly spread): partitions of pb blocks (64 / 32 / 16, the largest that
+// gives every warp two), all full ones first and the partial last ones longest first, claimed
+// from a counter. The prep kernel picks the static split below kStaticMaxBlocksPerWarp blocks
+// per warp on average.
 constexpr int kPartBlocks = TS_DECODE_PART_BLOCKS;
-constexpr int kMinPartBlocks = TS_DECODE_MIN_PART_BLOCKS;
+constexpr int kMinPartBlocks = 16;
+constexpr int kStaticMaxBlocksPerWarp = TS_DECODE_STATIC_MAX_BLOCKS;
 static_assert(kPartBlocks >= 2 && kPartBlocks <= 64, "a work item's table fits two registers per lane");
-static_assert(kMinPartBlocks >= 2 && kMinPartBlocks <= kPartBlocks, "bad partition bounds");
+// Upper bound of the grid's warps (SMs x warps per CTA), used to size the workspace.
+constexpr int kMaxGridWarps = 8192;
 constexpr float kLog2e = 1.4426950408889634f;
 
 struct DecodeArgs {
@@ -70,33 +83,46 @@ struct DecodeArgs {
   int group;  // query heads per KV head
   int64_t num_blocks;
   float scale_log2;
-  int* header;  // [0] work counter, [1] status, [2] blocks per work item this call
+  // [0] claim counter, [1] status, [2] 1 = dynamic claiming, [3] items to claim (dynamic) or
+  // groups (static)
+  int* header;
   int grid_warps;  // warps of the main kernel's grid
-  int* prefix;  // [batch + 1] partitions before sequence b
-  int4* part_info;  // [partition, in claim order] = (sequence, partition, slot partition, nparts)
-  int* part_ctx;     // [partition, in claim order] = context length of its sequence
+  // [batch + 1] partitions of one head before sequence b; sequence b's partition k of head h
+  // writes partial slot chunk_prefix[b] * H + h * parts_b + k, so a (sequence, head)'s partials
+  // are consecutive for the merge
+  int* chunk_prefix;
+  // [partition] = {(sequence, first block, blocks, index k in its sequence),
+  //                (chunk_prefix[sequence], partitions of the sequence, context length, 0)}
+  int4* part_info;
+  int* group_first;  // [groups + 1] first partition of each group (static split)
   int* arrive;  // [batch * num_kv_heads]
-  float* part_o;   // [slot][head_dim][NT * 8]
-  float2* part_ml;  // [slot][NT * 8]
+  float* part_o;   // [partition][head_dim][NT * 8]
+  float2* part_ml;  // [partition][NT * 8]
 };
 
 // Workspace layout (byte offsets), shared by the size query and the launcher.
 struct WsLayout {
-  size_t prefix, part_info, part_ctx, arrive, part_o, part_ml, total;
+  size_t chunk_prefix, part_info, group_first, arrive, part_o, part_ml, total;
 };
 
 inline size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
-WsLayout ws_layout(int batch, int hkv, int hd, int max_blocks, int nt) {
+int num_sms();
+
+// grid_warps: warps of the decode grid on the device the call runs on (its SMs x kWarps).
+WsLayout ws_layout(int batch, int hkv, int hd, int max_blocks, int nt, int grid_warps) {
   WsLayout w;
-  const size_t max_parts =
-      size_t(batch) * size_t((max_blocks + kMinPartBlocks - 1) / kMinPartBlocks);
-  const size_t slots = max_parts * size_t(hkv);
-  w.prefix = 256;
-  w.part_info = w.prefix + align256(sizeof(int) * (size_t(batch) + 1));
-  w.part_ctx = w.part_info + align256(sizeof(int4) * max_parts);
-  w.arrive = w.part_ctx + align256(sizeof(int) * max_parts);
-  w.part_o = w.arrive + align256(sizeof(int) * size_t(batch) * hkv);
+  // A sequence is cut at most once per kPartBlocks blocks and once per group boundary; each cut
+  // gives one partition per head (groups x heads <= grid warps).
+  const size_t bh = size_t(batch) * size_t(hkv);
+  const size_t slots = std::max(
+      bh * size_t((max_blocks + kPartBlocks - 1) / kPartBlocks + 1) + size_t(grid_warps),
+      bh * size_t((max_blocks + kMinPartBlocks - 1) / kMinPartBlocks));
+  w.chunk_prefix = 256;
+  w.part_info = w.chunk_prefix + align256(sizeof(int) * (size_t(batch) + 1));
+  w.group_first = w.part_info + align256(2 * sizeof(int4) * slots);
+  w.arrive = w.group_first + align256(sizeof(int) * (size_t(grid_warps) + 1));
+  w.part_o = w.arrive + align256(sizeof(int) * bh);
   w.part_ml = w.part_o + align256(sizeof(float) * slots * hd * nt * 8);
   w.total = w.part_ml + align256(sizeof(float2) * slots * nt * 8);
   return w;
@@ -130,103 +156,181 @@ __device__ __forceinline__ int block_exclusive_scan(int v, int* total, int* warp
   return incl - v + (warp > 0 ? warp_sums[warp - 1] : 0);
 }
 
-__device__ __forceinline__ int clamped_blocks(const DecodeArgs& a, int b) {
-  int ctx = a.context_lens[b];
-  ctx = ctx < 0 ? 0 : (ctx > a.max_blocks * kBlock ? a.max_blocks * kBlock : ctx);
-  return (ctx + kBlock - 1) / kBlock;
+
+__device__ __forceinline__ int blocks_of(int ctx) { return (ctx + kBlock - 1) / kBlock; }
+
+// The step's WB blocks in NG groups (0 < NG <= WB < 2^31): the first WB % NG groups hold
+// WB / NG + 1 blocks, the others WB / NG. 32-bit arithmetic only.
+struct GroupSplit {
+  int q, r;  // WB / NG, WB % NG
+  __device__ __forceinline__ GroupSplit(int WB, int NG) : q(WB / NG), r(WB % NG) {}
+  __device__ __forceinline__ int start(int g) const { return g * q + min(g, r); }
+  __device__ __forceinline__ int group_of(int u) const {
+    const int big = r * (q + 1);
+    return u < big ? u / (q + 1) : r + (u - big) / q;
+  }
+};
+
+// Calls f(group, group start, first block, end block) for every partition of blocks [u0, u1):
+// its pieces inside one group's range, each cut into kPartBlocks-block partitions, in order.
+template <typename F>
+__device__ __forceinline__ void for_each_chunk(int u0, int u1, const GroupSplit& gsp, F&& f) {
+  const int g0 = gsp.group_of(u0), g1 = gsp.group_of(u1 - 1);
+  int gs = gsp.start(g0);
+  for (int g = g0; g <= g1; ++g) {
+    const int gn = gsp.start(g + 1);
+    const int lo = max(u0, gs), hi = min(u1, gn);
+    for (int c = lo; c < hi; c += kPartBlocks) f(g, gs, c, min(hi, c + kPartBlocks));
+    gs = gn;
+  }
 }
 
-// One CTA: per-sequence partition counts -> prefix sums, and the descriptor of every work
-// partition in the order warps will claim them. With TS_DECODE_LPT the full partitions of all
-// sequences come first and the partial last partitions follow, longest first (counting sort),
-// so the kernel's tail is made of the shortest items. Also zeroes the counters and the output
-// rows of empty contexts.
-template <typename T>
-__global__ void __launch_bounds__(1024) decode_prep_kernel(DecodeArgs a, int row_elems) {
-  __shared__ int warp_sums[32];
-  __shared__ int hist[kPartBlocks], cursor[kPartBlocks];
-  __shared__ int chosen;
+constexpr int kPrepThreads = 1024;
+
+// Sequence b's context length, clamped to its block table.
+__device__ __forceinline__ int ctx_of(const DecodeArgs& a, int b) {
+  const int ctx = __ldg(a.context_lens + b), cap = a.max_blocks * kBlock;
+  return ctx < 0 ? 0 : (ctx > cap ? cap : ctx);
+}
+
+// Static split (small steps): groups of H warps, see kPartBlocks. run0: blocks before this
+// thread's first sequence b0; nblk: its cnt sequences' blocks.
+__device__ void prep_static(DecodeArgs& a, int* warp_sums, long long WB, int run0, int cnt,
+                            int b0) {
   const int B = a.batch;
-  const int per = (B + blockDim.x - 1) / blockDim.x;
-  const int b0 = threadIdx.x * per;
+  const int NG = int(min((long long)(a.grid_warps / a.num_kv_heads), WB));
+  const GroupSplit gsp(int(WB), NG > 0 ? NG : 1);
+  int c = 0;
+  int u = run0;
+  for (int i = 0; i < cnt; ++i) {
+    const int n = blocks_of(ctx_of(a, b0 + i));
+    if (n > 0) for_each_chunk(u, u + n, gsp, [&](int, int, int, int) { ++c; });
+    u += n;
+  }
+  int total = 0;
+  int runc = block_exclusive_scan(c, &total, warp_sums);
+  u = run0;
+  for (int i = 0; i < cnt; ++i) {
+    const int b = b0 + i;
+    a.chunk_prefix[b] = runc;
+    const int ctx = ctx_of(a, b), n = blocks_of(ctx);
+    int k = 0;
+    if (n > 0)
+      for_each_chunk(u, u + n, gsp, [&](int g, int gs, int lo, int hi) {
+        a.part_info[2 * (runc + k)] = make_int4(b, lo - u, hi - lo, k);
+        if (lo == gs) a.group_first[g] = runc + k;  // the partition that opens group g
+        ++k;
+      });
+    for (int m = 0; m < k; ++m) a.part_info[2 * (runc + m) + 1] = make_int4(runc, k, ctx, 0);
+    runc += k;
+    u += n;
+  }
+  if (threadIdx.x == 0) {
+    a.chunk_prefix[B] = total;
+    a.group_first[NG] = total;
+    a.header[2] = 0;
+    a.header[3] = NG;
+  }
+}
+
+// Dynamic claiming (large steps): partitions of pb blocks of every (sequence, head), pb the
+// largest of 64 / 32 / 16 that gives every warp two; full partitions first and the partial last
+// ones longest first (counting sort), so the kernel's tail is made of the shortest items.
+__device__ void prep_dynamic(DecodeArgs& a, int* warp_sums, int cnt, int b0) {
+  __shared__ int hist[kPartBlocks], cursor[kPartBlocks];
+  const int B = a.batch, H = a.num_kv_heads;
   if (threadIdx.x < kPartBlocks) hist[threadIdx.x] = 0;
-  // Items each candidate size would give; keep the largest size with >= 2 items per warp.
-  if (threadIdx.x == 0) chosen = kMinPartBlocks;
-  for (int cand = kPartBlocks; cand > kMinPartBlocks; cand /= 2) {
+  // pb: the largest candidate with two items per warp; its partition scan is kept.
+  int pb = kMinPartBlocks, run_p = 0, total_parts = 0;
+  for (int cand = kPartBlocks; cand >= kMinPartBlocks; cand /= 2) {
     int n = 0;
-    for (int i = 0; i < per; ++i)
-      if (b0 + i < B) n += (clamped_blocks(a, b0 + i) + cand - 1) / cand;
+    for (int i = 0; i < cnt; ++i) n += (blocks_of(ctx_of(a, b0 + i)) + cand - 1) / cand;
     int total = 0;
-    block_exclusive_scan(n, &total, warp_sums);
-    if (int64_t(total) * a.num_kv_heads >= 2 * int64_t(a.grid_warps)) {
-      if (threadIdx.x == 0) chosen = cand;
+    const int run = block_exclusive_scan(n, &total, warp_sums);
+    if (cand == kMinPartBlocks || int64_t(total) * H >= 2 * int64_t(a.grid_warps)) {
+      pb = cand;
+      run_p = run;
+      total_parts = total;
       break;
     }
   }
-  __syncthreads();
-  const int pbk = chosen;
-  int parts = 0, full = 0;
-  for (int i = 0; i < per; ++i) {
-    const int b = b0 + i;
-    if (b < B) {
-      const int nblk = clamped_blocks(a, b);
-      parts += (nblk + pbk - 1) / pbk;
-      full += nblk / pbk;
-    }
-  }
-  __syncthreads();
-  int total_parts = 0, total_full = 0;
-  int run_p = block_exclusive_scan(parts, &total_parts, warp_sums);
+  int full = 0;
+  for (int i = 0; i < cnt; ++i) full += blocks_of(ctx_of(a, b0 + i)) / pb;
+  int total_full = 0;
   int run_f = block_exclusive_scan(full, &total_full, warp_sums);
-  const int cap = a.max_blocks * kBlock;
-  for (int i = 0; i < per; ++i) {
-    const int b = b0 + i;
-    if (b < B) {
-      const int nblk = clamped_blocks(a, b);
-      const int ctx = min(max(a.context_lens[b], 0), cap);
-      const int np = (nblk + pbk - 1) / pbk, nf = nblk / pbk;
-      a.prefix[b] = run_p;
-      for (int p = 0; p < nf; ++p) {
-        const int idx = TS_DECODE_LPT ? run_f + p : run_p + p;
-        a.part_info[idx] = make_int4(b, p, run_p + p, np);
-        a.part_ctx[idx] = ctx;
-      }
-      if (nblk % pbk) atomicAdd(&hist[nblk % pbk], 1);
-      if (nblk == 0) {
-        T* o = static_cast<T*>(a.out) + int64_t(b) * row_elems;
-        for (int e = 0; e < row_elems; ++e) o[e] = ts::from_float<T>(0.f);
-      }
-      run_p += np;
-      run_f += nf;
-    }
+  // Partition p of sequence b -> claim position q (items q * H + h, one per head).
+  auto put = [&](int q, int b, int p, int n, int c0, int ctx) {
+    a.part_info[2 * q] = make_int4(b, p * pb, min(pb, n - p * pb), p);
+    a.part_info[2 * q + 1] = make_int4(c0, (n + pb - 1) / pb, ctx, 0);
+  };
+  const int run_p0 = run_p;
+  for (int i = 0; i < cnt; ++i) {
+    const int b = b0 + i, ctx = ctx_of(a, b), n = blocks_of(ctx);
+    a.chunk_prefix[b] = run_p;
+    for (int p = 0; p < n / pb; ++p) put(run_f + p, b, p, n, run_p, ctx);
+    if (n % pb) atomicAdd(&hist[n % pb], 1);
+    run_p += (n + pb - 1) / pb;
+    run_f += n / pb;
   }
   __syncthreads();
   if (threadIdx.x == 0) {
-    a.prefix[B] = total_parts;
     int off = total_full;
-    for (int sz = pbk - 1; sz >= 1; --sz) {  // longest partial partitions first
+    for (int sz = pb - 1; sz >= 1; --sz) {  // longest partial partitions first
       cursor[sz] = off;
       off += hist[sz];
     }
-    a.header[0] = 0;
-    a.header[1] = 0;
-    a.header[2] = pbk;
+    a.chunk_prefix[B] = total_parts;
+    a.header[2] = 1;
+    a.header[3] = total_parts * H;
   }
   __syncthreads();
-  for (int i = 0; i < per; ++i) {
-    const int b = b0 + i;
-    if (b < B) {
-      const int nblk = clamped_blocks(a, b);
-      const int r = nblk % pbk;
-      if (r) {
-        const int nf = nblk / pbk, pb = a.prefix[b];
-        const int idx = TS_DECODE_LPT ? atomicAdd(&cursor[r], 1) : pb + nf;
-        a.part_info[idx] = make_int4(b, nf, pb + nf, nf + 1);
-        a.part_ctx[idx] = min(max(a.context_lens[b], 0), cap);
-      }
-    }
+  int c0 = run_p0;
+  for (int i = 0; i < cnt; ++i) {
+    const int ctx = ctx_of(a, b0 + i), n = blocks_of(ctx);
+    if (n % pb) put(atomicAdd(&cursor[n % pb], 1), b0 + i, n / pb, n, c0, ctx);
+    c0 += (n + pb - 1) / pb;
   }
-  for (int i = threadIdx.x; i < B * a.num_kv_heads; i += blockDim.x) a.arrive[i] = 0;
+}
+
+// One CTA of kPrepThreads threads: chooses the split (static below kStaticMaxBlocksPerWarp blocks per
+// warp, dynamic above), writes the partition descriptors and the per-sequence partition
+// prefixes that place each (sequence, head)'s partial results, zeroes the claim counter, status
+// word and arrival counters, and writes the output rows of empty contexts.
+template <typename T>
+__global__ void __launch_bounds__(kPrepThreads) decode_prep_kernel(DecodeArgs a, int row_elems) {
+  __shared__ int warp_sums[32];
+  const int B = a.batch, H = a.num_kv_heads;
+  const int per = (B + blockDim.x - 1) / blockDim.x;
+  const int b0 = threadIdx.x * per;
+  const int cnt = max(0, min(per, B - b0));
+  int sum = 0;
+  for (int i = 0; i < cnt; ++i) sum += blocks_of(ctx_of(a, b0 + i));
+  // The step's total blocks (one reduction) decide the split; only the static split needs each
+  // thread's exclusive prefix.
+  __shared__ int total_smem;
+  if (threadIdx.x == 0) {
+    total_smem = 0;
+    a.header[0] = 0;
+    a.header[1] = 0;
+  }
+  __syncthreads();
+  const int wsum = __reduce_add_sync(0xffffffffu, unsigned(sum));
+  if (threadIdx.x % 32 == 0 && wsum) atomicAdd(&total_smem, wsum);
+  __syncthreads();
+  const long long WB = total_smem;
+  if (WB * H >= (long long)kStaticMaxBlocksPerWarp * a.grid_warps) {
+    prep_dynamic(a, warp_sums, cnt, b0);
+  } else {
+    int total_blocks = 0;
+    const int run0 = block_exclusive_scan(sum, &total_blocks, warp_sums);
+    prep_static(a, warp_sums, WB, run0, cnt, b0);
+  }
+  for (int i = 0; i < cnt; ++i)
+    if (ctx_of(a, b0 + i) == 0) {
+      T* o = static_cast<T*>(a.out) + int64_t(b0 + i) * row_elems;
+      for (int e = 0; e < row_elems; ++e) o[e] = ts::from_float<T>(0.f);
+    }
+  for (int i = threadIdx.x; i < B * H; i += blockDim.x) a.arrive[i] = 0;
 }
 
 // --------------------------------------------------------------------------- main kernel
@@ -264,22 +368,21 @@ __device__ __forceinline__ uint32_t tile_off(int t, int cg) {
 }
 
 struct ItemInfo {
-  int b, h, part, nparts, ctx, nblk, part_global;
+  int b, h, blk0, nparts, ctx, nblk, part_global, slot0;
 };
 
-// Work item (claim order) -> (sequence, partition, KV head): one descriptor load.
-__device__ __forceinline__ ItemInfo decode_item(const DecodeArgs& a, int item, int pb) {
+// (Partition, KV head) -> blocks to read and the partial-result slots of its (sequence, head).
+__device__ __forceinline__ ItemInfo decode_item(const DecodeArgs& a, int part, int h) {
   ItemInfo it;
-  const int pidx = item / a.num_kv_heads;
-  it.h = item - pidx * a.num_kv_heads;
-  const int4 pi = __ldg(a.part_info + pidx);
-  it.b = pi.x;
-  it.part = pi.y;
-  it.part_global = pi.z;
-  it.nparts = pi.w;
-  it.ctx = __ldg(a.part_ctx + pidx);
-  const int rem = (it.ctx + kBlock - 1) / kBlock - it.part * pb;
-  it.nblk = rem < pb ? rem : pb;
+  const int4 d = __ldg(a.part_info + 2 * part), e = __ldg(a.part_info + 2 * part + 1);
+  it.b = d.x;
+  it.h = h;
+  it.blk0 = d.y;
+  it.nblk = d.z;
+  it.nparts = e.y;
+  it.slot0 = e.x * a.num_kv_heads + h * it.nparts;
+  it.part_global = it.slot0 + d.w;
+  it.ctx = e.z;
   return it;
 }
 
@@ -301,8 +404,9 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
   const int g = lane >> 2, t = lane & 3;
   uint8_t* ring = smem + warp * G::kRingBytes;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kWarps * G::kRingBytes) + warp * S;
-  // Per stage: {item, block | invalid flag, sequence, partition}, {slot partition, nparts,
-  // context length, KV head} of the item the stage belongs to.
+  // Per stage: {partition, block | invalid flag, sequence, first block}, {first slot of its
+  // (sequence, head), partitions of that (sequence, head) | KV head << 16, context length,
+  // slot of the partition}.
   int4* meta =
       reinterpret_cast<int4*>(smem + kWarps * G::kRingBytes + G::kBarBytes) + warp * S * 2;
 
@@ -312,13 +416,24 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
   }
   __syncwarp();
 
-  const int total_items = __ldg(a.prefix + a.batch) * a.num_kv_heads;
-  const int pb = __ldg(a.header + 2);  // blocks per work item, chosen by the prep kernel
-  int* counter = a.header;
+  // This warp's work: items claimed from the counter (item = partition * H + head), or its
+  // group's partitions for its head (static split: warp gw = group * H + head).
+  const bool dynamic = __ldg(a.header + 2) != 0;
+  const int gw = blockIdx.x * kWarps + warp;
+  const int H = a.num_kv_heads;
+  int nxt = 0, part_end = 0, my_h = 0;
+  if (dynamic) {
+    part_end = __ldg(a.header + 3);
+    int c = 0;
+    if (lane == 0) c = atomicAdd(a.header, 1);
+    nxt = __shfl_sync(0xffffffffu, c, 0);
+  } else if (gw / H < __ldg(a.header + 3)) {
+    my_h = gw % H;
+    nxt = __ldg(a.group_first + gw / H);
+    part_end = __ldg(a.group_first + gw / H + 1);
+  }
 
   // ---- producer state (warp-uniform except p_table, one table entry per lane)
-  int nxt = 0;
-  if (lane == 0) nxt = atomicAdd(counter, 1);
   constexpr int TABW = (kPartBlocks + 31) / 32;  // table entries per lane
   int p_item = -1, p_blk = 0, p_nblk = 0;
   ItemInfo p_it{};
@@ -327,14 +442,19 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
 
   auto produce = [&](int s) {
     if (!p_done && p_blk == p_nblk) {
-      const int item = __shfl_sync(0xffffffffu, nxt, 0);
-      if (item < total_items) {
-        if (lane == 0) nxt = atomicAdd(counter, 1);
-        p_it = decode_item(a, item, pb);
-        p_item = item;
+      if (nxt < part_end) {
+        p_it = dynamic ? decode_item(a, nxt / H, nxt % H) : decode_item(a, nxt, my_h);
+        p_item = dynamic ? nxt : nxt * H + my_h;
+        if (dynamic) {
+          int c = 0;
+          if (lane == 0) c = atomicAdd(a.header, 1);
+          nxt = __shfl_sync(0xffffffffu, c, 0);
+        } else {
+          ++nxt;
+        }
         p_nblk = p_it.nblk;
         p_blk = 0;
-        const int32_t* row = a.block_tables + int64_t(p_it.b) * a.max_blocks + p_it.part * pb;
+        const int32_t* row = a.block_tables + int64_t(p_it.b) * a.max_blocks + p_it.blk0;
 #pragma unroll
         for (int w = 0; w < TABW; ++w)
           p_table[w] = lane + 32 * w < p_it.nblk ? __ldg(row + lane + 32 * w) : 0;
@@ -353,8 +473,9 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
     const int phys = __shfl_sync(0xffffffffu, tab, p_blk & 31);
     const bool valid = phys >= 0 && int64_t(phys) < a.num_blocks;
     if (lane == 0) {
-      meta[2 * s] = make_int4(p_item, valid ? p_blk : (p_blk | 0x40000000), p_it.b, p_it.part);
-      meta[2 * s + 1] = make_int4(p_it.part_global, p_it.nparts, p_it.ctx, p_it.h);
+      meta[2 * s] = make_int4(p_item, valid ? p_blk : (p_blk | 0x40000000), p_it.b, p_it.blk0);
+      meta[2 * s + 1] = make_int4(p_it.slot0, p_it.nparts | (p_it.h << 16), p_it.ctx,
+                                  p_it.part_global);  // nparts < 2^16, h < 2^15
       if (valid) {
         ts::mbar_arrive_expect_tx(&bars[s], G::kStageBytes);
         const int row = (phys * a.num_kv_heads + p_it.h) * kBlock;
@@ -390,11 +511,12 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
   auto start_item = [&](const int4& m0, const int4& m1) {
     cur_item = m0.x;
     it.b = m0.z;
-    it.part = m0.w;
-    it.part_global = m1.x;
-    it.nparts = m1.y;
+    it.blk0 = m0.w;
+    it.slot0 = m1.x;
+    it.nparts = m1.y & 0xffff;
+    it.h = m1.y >> 16;
     it.ctx = m1.z;
-    it.h = m1.w;
+    it.part_global = m1.w;
     const T* qb = static_cast<const T*>(a.query) + int64_t(it.b) * a.q_stride;
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) {
@@ -448,7 +570,7 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
       return;
     }
     // Partial result of one partition: unnormalised O^T, running max and sum.
-    const int64_t slot = int64_t(it.part_global) * a.num_kv_heads + it.h;
+    const int64_t slot = it.part_global;
     float* po = a.part_o + slot * D * NT8;
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt)
@@ -475,17 +597,17 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
     // Last partition of (b, h) to finish: merge all of them.
     __threadfence();
     const int hd = lane % NT8;  // fixed head per lane in the [D][NT8] layout
-    const int64_t slot0 = int64_t(__ldg(a.prefix + it.b)) * a.num_kv_heads + it.h;
+    const int64_t slot0 = it.slot0;
     float mx = -INFINITY;
     for (int p = 0; p < it.nparts; ++p)
-      mx = fmaxf(mx, __ldcg(&a.part_ml[(slot0 + int64_t(p) * a.num_kv_heads) * NT8 + hd].x));
+      mx = fmaxf(mx, __ldcg(&a.part_ml[(slot0 + p) * NT8 + hd].x));
     constexpr int PER = D * NT8 / 32;
     float acc[PER];
 #pragma unroll
     for (int i = 0; i < PER; ++i) acc[i] = 0.f;
     float lsum = 0.f;
     for (int p = 0; p < it.nparts; ++p) {
-      const int64_t sl = slot0 + int64_t(p) * a.num_kv_heads;
+      const int64_t sl = slot0 + p;
       const float2 ml = __ldcg(&a.part_ml[sl * NT8 + hd]);
       const float w = ml.x == -INFINITY ? 0.f : exp2f(ml.x - mx);
       lsum += w * ml.y;
@@ -522,7 +644,7 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
     if ((md.y & 0x40000000) == 0) {
       const uint32_t kb = ts::smem_u32(ring + s * G::kStageBytes);
       const uint32_t vb = kb + G::kTileBytes;
-      const int tok0 = (it.part * pb + md.y) * kBlock;
+      const int tok0 = (it.blk0 + md.y) * kBlock;
       const int nvalid = it.ctx - tok0;
 
       // S^T[token][head] = K Q^T
@@ -671,7 +793,7 @@ int launch_fast(const DecodeArgs& a, const CUtensorMap& km, const CUtensorMap& v
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, G::kSmemBytes);
     if (dev >= 0 && dev < 64) attr_done[dev] = true;
   }
-  decode_prep_kernel<T><<<1, 1024, 0, s>>>(a, a.num_q_heads * D);
+  decode_prep_kernel<T><<<1, kPrepThreads, 0, s>>>(a, a.num_q_heads * D);
   kern<<<num_sms(), kWarps * 32, G::kSmemBytes, s>>>(km, vm, a);
   return ts::launch_status("paged_decode");
 }
@@ -682,6 +804,7 @@ bool fast_path(int hq, int hkv, int hd, int bs, int dtype, int64_t num_blocks, c
   if (dtype != TS_BFLOAT16 && dtype != TS_FLOAT16) return false;
   if (bs != kBlock || (hd != 64 && hd != 128)) return false;
   if (hkv <= 0 || hq % hkv != 0 || hq / hkv > 16) return false;
+  if (hkv > num_sms() * kWarps) return false;  // one warp per KV head in a group
   if (num_blocks * hkv * kBlock >= (int64_t(1) << 31)) return false;
   if ((reinterpret_cast<uint64_t>(kp) | reinterpret_cast<uint64_t>(vp)) % 16) return false;
   if ((reinterpret_cast<uint64_t>(q) | reinterpret_cast<uint64_t>(out)) % 4 || q_stride % 2)
@@ -708,7 +831,7 @@ extern "C" size_t ts_paged_decode_workspace_size(int32_t batch, int32_t num_q_he
       (head_dim != 64 && head_dim != 128) || num_q_heads / num_kv_heads > 16)
     return 0;
   const int nt = num_q_heads / num_kv_heads > 8 ? 2 : 1;
-  return ws_layout(batch, num_kv_heads, head_dim, max_blocks_per_seq, nt).total;
+  return ws_layout(batch, num_kv_heads, head_dim, max_blocks_per_seq, nt, num_sms() * kWarps).total;
 }
 
 extern "C" int ts_paged_decode(void* out, const void* query, int64_t query_token_stride,
@@ -741,9 +864,12 @@ extern "C" int ts_paged_decode(void* out, const void* query, int64_t query_token
                                         block_size, num_blocks, scale, dtype, s);
   if (batch > 8192)
     return ts::set_error(TS_ERR_UNSUPPORTED, "paged_decode: batch %d above 8192", batch);
+  if (int64_t(batch) * max_blocks_per_seq >= (int64_t(1) << 31) ||
+      max_blocks_per_seq > (1 << 20) || num_sms() * kWarps > kMaxGridWarps)
+    return ts::set_error(TS_ERR_UNSUPPORTED, "paged_decode: batch x max_blocks or grid too large");
   const int group = num_q_heads / num_kv_heads;
   const int nt = group > 8 ? 2 : 1;
-  const WsLayout w = ws_layout(batch, num_kv_heads, head_dim, max_blocks_per_seq, nt);
+  const WsLayout w = ws_layout(batch, num_kv_heads, head_dim, max_blocks_per_seq, nt, num_sms() * kWarps);
   if (workspace == nullptr || workspace_bytes < w.total)
     return ts::set_error(TS_ERR_WORKSPACE_TOO_SMALL,
                          "paged_decode: workspace of %zu bytes, need %zu", workspace_bytes,
@@ -771,9 +897,9 @@ extern "C" int ts_paged_decode(void* out, const void* query, int64_t query_token
   a.scale_log2 = scale * kLog2e;
   a.grid_warps = num_sms() * kWarps;
   a.header = reinterpret_cast<int*>(ws);
-  a.prefix = reinterpret_cast<int*>(ws + w.prefix);
+  a.chunk_prefix = reinterpret_cast<int*>(ws + w.chunk_prefix);
   a.part_info = reinterpret_cast<int4*>(ws + w.part_info);
-  a.part_ctx = reinterpret_cast<int*>(ws + w.part_ctx);
+  a.group_first = reinterpret_cast<int*>(ws + w.group_first);
   a.arrive = reinterpret_cast<int*>(ws + w.arrive);
   a.part_o = reinterpret_cast<float*>(ws + w.part_o);
   a.part_ml = reinterpret_cast<float2*>(ws + w.part_ml);
@@ -863,9 +989,13 @@ extern "C" int ts_paged_decode_no_alloc(void* out, const void* query, int64_t qu
                                         block_size, num_blocks, scale, dtype, s);
   if (batch > 8192)
     return ts::set_error(TS_ERR_UNSUPPORTED, "paged_decode_no_alloc: batch %d above 8192", batch);
+  if (int64_t(batch) * max_blocks_per_seq >= (int64_t(1) << 31) ||
+      max_blocks_per_seq > (1 << 20) || num_sms() * kWarps > kMaxGridWarps)
+    return ts::set_error(TS_ERR_UNSUPPORTED,
+                         "paged_decode_no_alloc: batch x max_blocks or grid too large");
   const int group = num_q_heads / num_kv_heads;
   const int nt = group > 8 ? 2 : 1;
-  const WsLayout w = ws_layout(batch, num_kv_heads, head_dim, max_blocks_per_seq, nt);
+  const WsLayout w = ws_layout(batch, num_kv_heads, head_dim, max_blocks_per_seq, nt, num_sms() * kWarps);
   if (w.total > kStaticScratchBytes)
     return ts::set_error(TS_ERR_WORKSPACE_TOO_SMALL,
                          "paged_decode_no_alloc: these sizes need %zu bytes of scratch but the "
@@ -898,9 +1028,9 @@ extern "C" int ts_paged_decode_no_alloc(void* out, const void* query, int64_t qu
   a.scale_log2 = scale * kLog2e;
   a.grid_warps = num_sms() * kWarps;
   a.header = reinterpret_cast<int*>(ws);
-  a.prefix = reinterpret_cast<int*>(ws + w.prefix);
+  a.chunk_prefix = reinterpret_cast<int*>(ws + w.chunk_prefix);
   a.part_info = reinterpret_cast<int4*>(ws + w.part_info);
-  a.part_ctx = reinterpret_cast<int*>(ws + w.part_ctx);
+  a.group_first = reinterpret_cast<int*>(ws + w.group_first);
   a.arrive = reinterpret_cast<int*>(ws + w.arrive);
   a.part_o = reinterpret_cast<float*>(ws + w.part_o);
   a.part_ml = reinterpret_cast<float2*>(ws + w.part_ml);
