@@ -133,6 +133,8 @@ __host__ __forceinline__ bool aligned16(const void* p) {
 
 // ------------------------------------------------------------------------- RoPE + K1
 
+constexpr int kMaxHalf = 256;  // head_dim <= 512
+
 // One CTA per token; one thread per (head, dim pair i in [0, D/2)).
 template <typename T>
 __global__ void rope_and_cache_kernel(const T* __restrict__ qkv, int64_t qkv_stride,
@@ -147,6 +149,13 @@ __global__ void rope_and_cache_kernel(const T* __restrict__ qkv, int64_t qkv_str
   const T* row = qkv + t * qkv_stride;
   const float pos = float(__ldg(positions + t));
   const int half = d / 2;
+  __shared__ float cs[2][kMaxHalf];  // cos / sin per angle, rounded to the dtype
+  for (int i = threadIdx.x; i < half; i += blockDim.x) {
+    const float ang = pos * __ldg(inv_freq + i);
+    cs[0][i] = ts::to_float(rnd<T>(cosf(ang)));
+    cs[1][i] = ts::to_float(rnd<T>(sinf(ang)));
+  }
+  __syncthreads();
   const int64_t slot = __ldg(slots + t);
   const bool write_kv = slot >= 0 && slot < num_slots;
   if (slot >= num_slots && error_flag != nullptr && threadIdx.x == 0) atomicExch(error_flag, 1);
@@ -156,10 +165,8 @@ __global__ void rope_and_cache_kernel(const T* __restrict__ qkv, int64_t qkv_str
     const int h = j / half, i = j - (j / half) * half;
     if (h < hq + hkv) {
       // cos/sin of emb = cat(freqs, freqs): dims i and i + D/2 share the angle.
-      const float ang = pos * __ldg(inv_freq + i);
-      const T c = rnd<T>(cosf(ang)), s = rnd<T>(sinf(ang));
       const float x1 = ts::to_float(row[h * d + i]), x2 = ts::to_float(row[h * d + i + half]);
-      const float cf = ts::to_float(c), sf = ts::to_float(s);
+      const float cf = cs[0][i], sf = cs[1][i];
       // rotate_half(x) = cat(-x2, x1)
       const T y1 = rnd<T>(ts::to_float(rnd<T>(__fmul_rn(x1, cf))) +
                           ts::to_float(rnd<T>(__fmul_rn(-x2, sf))));
@@ -199,6 +206,14 @@ __global__ void rope_and_cache_vec_kernel(const T* __restrict__ qkv, int64_t qkv
   const T* row = qkv + t * qkv_stride;
   const float pos = float(__ldg(positions + t));
   const int half = d / 2, cpr = half / E;
+  // cos / sin of this token's angles, rounded to the dtype, computed once for every head.
+  __shared__ float cs[2][kMaxHalf];
+  for (int i = threadIdx.x; i < half; i += blockDim.x) {
+    const float ang = pos * __ldg(inv_freq + i);
+    cs[0][i] = ts::to_float(rnd<T>(cosf(ang)));
+    cs[1][i] = ts::to_float(rnd<T>(sinf(ang)));
+  }
+  __syncthreads();
   const int64_t slot = __ldg(slots + t);
   const bool write_kv = slot >= 0 && slot < num_slots;
   if (slot >= num_slots && error_flag != nullptr && threadIdx.x == 0) atomicExch(error_flag, 1);
@@ -213,8 +228,7 @@ __global__ void rope_and_cache_vec_kernel(const T* __restrict__ qkv, int64_t qkv
     if (h < hq + hkv) {
 #pragma unroll
       for (int e = 0; e < E; ++e) {
-        const float ang = pos * __ldg(inv_freq + i0 + e);
-        const float cf = ts::to_float(rnd<T>(cosf(ang))), sf = ts::to_float(rnd<T>(sinf(ang)));
+        const float cf = cs[0][i0 + e], sf = cs[1][i0 + e];
         const float x1 = ts::to_float(a.v[e]), x2 = ts::to_float(b.v[e]);
         y1.v[e] = rnd<T>(ts::to_float(rnd<T>(__fmul_rn(x1, cf))) +
                          ts::to_float(rnd<T>(__fmul_rn(-x2, sf))));
@@ -327,6 +341,8 @@ extern "C" int ts_rope_and_cache(const void* qkv, int64_t qkv_token_stride, void
   if (num_tokens < 0 || num_q_heads <= 0 || num_kv_heads <= 0 || head_dim <= 0 ||
       head_dim % 2 || block_size <= 0 || num_blocks <= 0 || ts::dtype_size(dtype) == 0)
     return ts::set_error(TS_ERR_INVALID_ARGUMENT, "rope_and_cache: bad sizes or dtype");
+  if (head_dim > 2 * kMaxHalf)
+    return ts::set_error(TS_ERR_UNSUPPORTED, "rope_and_cache: head_dim above %d", 2 * kMaxHalf);
   if (qkv_token_stride < int64_t(num_q_heads + 2 * num_kv_heads) * head_dim)
     return ts::set_error(TS_ERR_INVALID_ARGUMENT, "rope_and_cache: qkv stride too small");
   if (num_tokens == 0) return ts::ok();
