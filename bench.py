@@ -59,6 +59,12 @@ def parse() -> argparse.Namespace:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--pool-blocks", type=int, default=65536)
     ap.add_argument("--skip-e2e", action="store_true", help="profiling runs only")
+    ap.add_argument("--collective", choices=["fused", "nccl"], default="fused",
+                    help="decode70b at N>1: decode writing every rank's output buffer over "
+                         "NVLink (fused) or decode + NCCL all-gather")  # fmt: skip
+    ap.add_argument("--shard-of", type=int, default=1,
+                    help="decode70b on 1 GPU: run rank 0's share of an N-way KV-head split "
+                         "(no collective), to measure the per-rank kernel alone")  # fmt: skip
     return ap.parse_args()
 
 
@@ -570,7 +576,8 @@ def run_decode70b(args: argparse.Namespace, world: int, rank: int, local: int) -
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180), device_id=dev)
     ops.load_library()
     case = decode70b_workload(seed=0)  # identical tables on every rank
-    sh = shard_heads(case.num_q_heads, case.num_kv_heads, world, rank)
+    split = world if world > 1 else max(1, args.shard_of)
+    sh = shard_heads(case.num_q_heads, case.num_kv_heads, split, rank)
     B, hq_r, hkv_r, d, nb = case.batch, sh.num_q_heads, sh.num_kv_heads, 128, case.num_blocks
     dt = torch.bfloat16
     layers = 80
@@ -599,16 +606,33 @@ def run_decode70b(args: argparse.Namespace, world: int, rank: int, local: int) -
     made = [torch.cuda.Event() for _ in range(nbuf)]
     freed = [torch.cuda.Event() for _ in range(nbuf)]
     kv_bytes_rank = case.kv_bytes(2) * hkv_r // case.num_kv_heads
+    fused = world > 1 and args.collective == "fused"
+    pg = None
+    if fused:
+        from tokenserve_b200.peer import PeerGather
+
+        pg = PeerGather(B, hq_r, d, dt, nbuf=nbuf)
 
     def step(dec_ev=None, ag_ev=None) -> None:  # type: ignore[no-untyped-def]
         for li in range(layers):
             p = li % nbuf
             pool = pools[li % resident]
-            if li >= nbuf and world > 1:
+            if li >= nbuf and world > 1 and not fused:
                 comp.wait_event(freed[p])  # the gather of layer li-nbuf has read outs[p]
             ops.reshape_and_cache(knew, vnew, pool[0], pool[1], slots)
             if dec_ev is not None:
                 dec_ev[li][0].record(comp)
+            if fused:
+                # K2 writes this rank's heads into every rank's buffer p over NVLink; the wait
+                # (a one-block kernel on this stream) holds later work until all ranks have.
+                epoch = pg.decode(p, q, pool[0], pool[1], bt, cl, d**-0.5, ws)
+                if dec_ev is not None:
+                    dec_ev[li][1].record(comp)
+                    ag_ev[li][0].record(comp)
+                pg.wait(epoch)
+                if ag_ev is not None:
+                    ag_ev[li][1].record(comp)
+                continue
             ops.paged_decode(outs[p], q, pool[0], pool[1], bt, cl, d**-0.5, ws)
             if dec_ev is not None:
                 dec_ev[li][1].record(comp)
@@ -678,8 +702,15 @@ def run_decode70b(args: argparse.Namespace, world: int, rank: int, local: int) -
                 "context": "log-normal median 4096 sigma 1.0 clipped 16..32768",
                 "pool_blocks": nb, "pool": "85% of the batch's demand; sequences past it wait",
                 "resident_layer_pools_per_rank": resident,
-                "parallelism": f"KV-head sharding x{world} (Hkv/N={hkv_r}, Hq/N={hq_r})",
-                "collective": "per-layer all_gather of [B, Hq/N, D] on a second stream" if world > 1 else "none",
+                "parallelism": (f"KV-head sharding x{world} (Hkv/N={hkv_r}, Hq/N={hq_r})" if world > 1
+                                else f"one GPU running rank 0's share of an {split}-way split "
+                                     f"(Hkv={hkv_r}, Hq={hq_r}), no collective" if split > 1
+                                else "single GPU"),
+                "collective": ("none" if world == 1 else
+                               "fused: K2 stores each rank's [B, Hq/N, D] rows into every rank's "
+                               "[B, Hq, D] buffer over NVLink, then a bounded device wait for "
+                               "all ranks' epoch flag" if fused else
+                               "per-layer NCCL all_gather of [B, Hq/N, D] on a second stream"),
             },
             "per_rank_frac_of_hbm_peak": round(kv_bytes_rank * layers * args.steps / elapsed / 1e9 / peak, 4),
             "roofline": {
@@ -689,12 +720,19 @@ def run_decode70b(args: argparse.Namespace, world: int, rank: int, local: int) -
                 "frac": round((kv_bytes_rank + 2 * B * hq_r * d * 2) / dec_t / 1e9 / peak, 4),
                 "avg_launch_us": round(dec_t * 1e6, 2),
             },
-            "allgather": ({"bytes_per_layer": ag_bytes, "avg_us": round(ag_t * 1e6, 2),
-                           "algbw_gbs": round(ag_bytes / ag_t / 1e9, 1)} if world > 1 else None),
-            "gpu_launches": (3 * layers + (2 if world > 1 else 0) * layers) * args.steps,
+            "allgather": (None if world == 1 else
+                          {"bytes_per_layer": ag_bytes, "wait_after_decode_us": round(ag_t * 1e6, 2),
+                           "note": "the gather is the decode's own stores; this is the wait "
+                                   "kernel on the compute stream (rank skew + last stores)"}
+                          if fused else
+                          {"bytes_per_layer": ag_bytes, "avg_us": round(ag_t * 1e6, 2),
+                           "algbw_gbs": round(ag_bytes / ag_t / 1e9, 1)}),
+            "gpu_launches": ((4 if fused else 3 + (2 if world > 1 else 0)) * layers) * args.steps,
             "clocks": clocks.summary(),
         }  # fmt: skip
         print(json.dumps(line), flush=True)
+    if pg is not None:
+        pg.close()
     if world > 1:
         dist.barrier(device_ids=[local])
         dist.destroy_process_group()

@@ -223,6 +223,45 @@ int ts_verify_tags(const int32_t* tag_pool, const int32_t* block_tables,
                    int32_t* mismatch_pos, void* stream);
 
 /*
+ * K2 of one rank of a KV-head-sharded model, fused with the all-gather of its output.
+ *
+ * Replaces: the per-layer all-gather of attention outputs in the sharded configuration (the
+ * reference runs a single process; the sharded layout is this backend's: rank r of `world`
+ * holds KV heads [r*Hkv/world, (r+1)*Hkv/world) and their query heads, under replicated block
+ * tables). Arguments as ts_paged_decode for this rank's heads (num_q_heads / num_kv_heads are the
+ * rank's counts), except the output: each of dst_outs[0..world) is a rank's full output
+ * [batch][world * num_q_heads][head_dim], and this rank's rows land at head offset
+ * rank * num_q_heads in every one of them (stores over NVLink for the peers). The grid's last
+ * CTA then writes `epoch` (non-zero, increasing per call) into signals[r][rank] for every r.
+ * dst_outs and signals are device arrays of device pointers (peer buffers mapped with
+ * ts_ipc_open); the tensor-core decode path is required (TS_ERR_UNSUPPORTED otherwise).
+ */
+int ts_paged_decode_peer(void* const* dst_outs, int32_t world, int32_t rank,
+                         int32_t* const* signals, uint32_t epoch, const void* query,
+                         int64_t query_token_stride, const void* key_pool, const void* value_pool,
+                         const int32_t* block_tables, int32_t max_blocks_per_seq,
+                         const int32_t* context_lens, int32_t batch, int32_t num_q_heads,
+                         int32_t num_kv_heads, int32_t head_dim, int32_t block_size,
+                         int64_t num_blocks, float scale, int32_t dtype, void* workspace,
+                         size_t workspace_bytes, void* stream);
+
+/*
+ * Waits on the device until local_signals[r] >= epoch for every r < world (every rank's
+ * ts_paged_decode_peer of that epoch has finished writing into this rank's buffer). The wait
+ * is bounded (about a second); on timeout *status (device int32) is set to 3 and the kernel
+ * returns, leaving the context usable.
+ */
+int ts_wait_peers(const int32_t* local_signals, int32_t world, uint32_t epoch, int32_t* status,
+                  void* stream);
+
+/* Device buffers shared between the ranks' processes, and their CUDA IPC handles (64 bytes). */
+int ts_peer_alloc(size_t bytes, void** ptr);
+int ts_peer_free(void* ptr);
+int ts_ipc_get_handle(const void* ptr, void* handle);
+int ts_ipc_open(const void* handle, void** ptr);
+int ts_ipc_close(void* ptr);
+
+/*
  * Fused element-wise parts of a Llama decoder layer used by the paged model runner. They
  * replace transformers 5.5.0 modules (models/llama/modeling_llama.py) that tokenserve's
  * HFBackend runs per sequence (src/tokenserve/backends/hf.py:71), with the same rounding points.

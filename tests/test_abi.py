@@ -76,6 +76,13 @@ def test_argument_errors_are_reported_before_any_launch(lib: ctypes.CDLL) -> Non
     rc = lib.ts_swap_blocks(None, 6400, 100, None, 256, 4, 2, 64, None, 1, None, None)
     assert rc == -1 and b"null pointer" in lib.ts_last_error()
     assert lib.ts_swap_blocks(None, 6400, 100, None, 256, 4, 2, 64, None, 0, None, None) == 0
+    rc = lib.ts_paged_decode_peer(None, 0, 0, None, 1, None, 4096, None, None, None, 8, None, 2,
+                                  32, 8, 128, 16, 100, 0.1, ops.TS_BFLOAT16, None, 0, None)  # fmt: skip
+    assert rc == -1 and b"paged_decode_peer: bad world" in lib.ts_last_error()
+    rc = lib.ts_paged_decode_peer(None, 2, 0, None, 0, None, 4096, None, None, None, 8, None, 2,
+                                  32, 8, 128, 16, 100, 0.1, ops.TS_BFLOAT16, None, 0, None)  # fmt: skip
+    assert rc == -1 and b"epoch" in lib.ts_last_error()
+    assert lib.ts_wait_peers(None, 2, 1, None, None) == -1
     # Empty work is a successful no-op and clears the message.
     assert lib.ts_paged_prefill(None, None, 4096, None, None, None, 1, None, None, 0, 0, 0, 32,
                                 8, 128, 16, 10, 0.1, ops.TS_BFLOAT16, None) == 0  # fmt: skip

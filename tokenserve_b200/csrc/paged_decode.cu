@@ -24,6 +24,7 @@
 #include <cudaTypedefs.h>
 
 #include <algorithm>
+#include <cstring>
 #include <mutex>
 
 #include "common.cuh"
@@ -71,7 +72,19 @@ constexpr int kMaxGridWarps = 8192;
 constexpr float kLog2e = 1.4426950408889634f;
 
 struct DecodeArgs {
+  // Output rows: sequence b, query head j (of this call's num_q_heads) goes to
+  // dst + b * out_row_stride + (out_head0 + j) * head_dim for dst = out, or, with n_out > 0,
+  // for every dst in outs[0..n_out) (the ranks' full buffers of a KV-head-sharded model).
   void* out;
+  void* const* outs;  // device array of n_out pointers, or nullptr
+  int n_out;
+  int64_t out_row_stride;  // elements
+  int out_head0;
+  // Completion signal (n_out > 0): the grid's last CTA stores `epoch` into
+  // signals[r][signal_index] for every r < n_out, after every CTA's output stores.
+  int* const* signals;
+  int signal_index;
+  unsigned epoch;
   const void* query;
   int64_t q_stride;
   const int32_t* block_tables;
@@ -84,7 +97,7 @@ struct DecodeArgs {
   int64_t num_blocks;
   float scale_log2;
   // [0] claim counter, [1] status, [2] 1 = dynamic claiming, [3] items to claim (dynamic) or
-  // groups (static)
+  // groups (static), [4] CTAs finished (completion signal)
   int* header;
   int grid_warps;  // warps of the main kernel's grid
   // [batch + 1] partitions of one head before sequence b; sequence b's partition k of head h
@@ -312,6 +325,7 @@ __global__ void __launch_bounds__(kPrepThreads) decode_prep_kernel(DecodeArgs a,
     total_smem = 0;
     a.header[0] = 0;
     a.header[1] = 0;
+    a.header[4] = 0;
   }
   __syncthreads();
   const int wsum = __reduce_add_sync(0xffffffffu, unsigned(sum));
@@ -326,11 +340,20 @@ __global__ void __launch_bounds__(kPrepThreads) decode_prep_kernel(DecodeArgs a,
     prep_static(a, warp_sums, WB, run0, cnt, b0);
   }
   for (int i = 0; i < cnt; ++i)
-    if (ctx_of(a, b0 + i) == 0) {
-      T* o = static_cast<T*>(a.out) + int64_t(b0 + i) * row_elems;
-      for (int e = 0; e < row_elems; ++e) o[e] = ts::from_float<T>(0.f);
-    }
+    if (ctx_of(a, b0 + i) == 0)
+      for (int o = 0; o < (a.n_out > 0 ? a.n_out : 1); ++o) {
+        T* dst = static_cast<T*>(a.n_out > 0 ? a.outs[o] : a.out) +
+                 int64_t(b0 + i) * a.out_row_stride + int64_t(a.out_head0) * (row_elems / a.num_q_heads);
+        for (int e = 0; e < row_elems; ++e) dst[e] = ts::from_float<T>(0.f);
+      }
   for (int i = threadIdx.x; i < B * H; i += blockDim.x) a.arrive[i] = 0;
+}
+
+// Output row (sequence b, query head j) in destination o (< max(n_out, 1)).
+template <typename T, int D>
+__device__ __forceinline__ T* out_row(const DecodeArgs& a, int o, int b, int j) {
+  T* base = static_cast<T*>(a.n_out == 0 ? a.out : a.outs[o]);
+  return base + int64_t(b) * a.out_row_stride + int64_t(a.out_head0 + j) * D;
 }
 
 // --------------------------------------------------------------------------- main kernel
@@ -550,20 +573,24 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
         l_run[nt][j] = l;
       }
     if (it.nparts == 1) {
-      T* ob = static_cast<T*>(a.out) + (int64_t(it.b) * a.num_q_heads + it.h * a.group) * D;
+      const int n_dst = a.n_out > 0 ? a.n_out : 1;
+#pragma unroll 1
+      for (int o = 0; o < n_dst; ++o) {
 #pragma unroll
-      for (int nt = 0; nt < NT; ++nt) {
-        const float i0 = l_run[nt][0] > 0.f ? 1.f / l_run[nt][0] : 0.f;
-        const float i1 = l_run[nt][1] > 0.f ? 1.f / l_run[nt][1] : 0.f;
-        const int head = nt * 8 + g;  // after the transpose a lane owns one head
+        for (int nt = 0; nt < NT; ++nt) {
+          const float i0 = l_run[nt][0] > 0.f ? 1.f / l_run[nt][0] : 0.f;
+          const float i1 = l_run[nt][1] > 0.f ? 1.f / l_run[nt][1] : 0.f;
+          const int head = nt * 8 + g;  // after the transpose a lane owns one head
+          uint32_t* orow =
+              reinterpret_cast<uint32_t*>(out_row<T, D>(a, o, it.b, it.h * a.group + head));
 #pragma unroll
-        for (int mt = 0; mt < MTILES; ++mt) {
-          const uint32_t lo = movmatrix_pack<Mma>(oacc[nt][mt][0] * i0, oacc[nt][mt][1] * i1);
-          const uint32_t hi = movmatrix_pack<Mma>(oacc[nt][mt][2] * i0, oacc[nt][mt][3] * i1);
-          if (head < a.group) {
-            uint32_t* orow = reinterpret_cast<uint32_t*>(ob + int64_t(head) * D);
-            orow[(mt * 16 + 2 * t) / 2] = lo;
-            orow[(mt * 16 + 8 + 2 * t) / 2] = hi;
+          for (int mt = 0; mt < MTILES; ++mt) {
+            const uint32_t lo = movmatrix_pack<Mma>(oacc[nt][mt][0] * i0, oacc[nt][mt][1] * i1);
+            const uint32_t hi = movmatrix_pack<Mma>(oacc[nt][mt][2] * i0, oacc[nt][mt][3] * i1);
+            if (head < a.group) {
+              orow[(mt * 16 + 2 * t) / 2] = lo;
+              orow[(mt * 16 + 8 + 2 * t) / 2] = hi;
+            }
           }
         }
       }
@@ -617,10 +644,13 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
     }
     const float inv = lsum > 0.f ? 1.f / lsum : 0.f;
     if (hd < a.group) {
-      T* orow = static_cast<T*>(a.out) +
-                (int64_t(it.b) * a.num_q_heads + it.h * a.group + hd) * D;
+      const int n_dst = a.n_out > 0 ? a.n_out : 1;
+#pragma unroll 1
+      for (int o = 0; o < n_dst; ++o) {
+        T* orow = out_row<T, D>(a, o, it.b, it.h * a.group + hd);
 #pragma unroll
-      for (int i = 0; i < PER; ++i) orow[(lane + 32 * i) / NT8] = ts::from_float<T>(acc[i] * inv);
+        for (int i = 0; i < PER; ++i) orow[(lane + 32 * i) / NT8] = ts::from_float<T>(acc[i] * inv);
+      }
     }
     if (lane == 0) a.arrive[it.b * a.num_kv_heads + it.h] = 0;
   };
@@ -728,9 +758,39 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
       const uint32_t kk = k + j;
       ts::mbar_wait_bounded(&bars[kk % S], (kk / S) & 1);
     }
-    return;
+  } else if (cur_item >= 0) {
+    finish_item();
   }
-  if (cur_item >= 0) finish_item();
+  if (a.n_out > 0) {
+    // Every thread's output stores (local and peer) are made visible system-wide before its
+    // CTA counts itself done; the last CTA then publishes the epoch to every rank.
+    __threadfence_system();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      const int done = atomicAdd(a.header + 4, 1);
+      if (done == int(gridDim.x) - 1) {
+        __threadfence_system();
+        for (int r = 0; r < a.n_out; ++r) {
+          int* flag = a.signals[r] + a.signal_index;
+          asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(flag), "r"(a.epoch) : "memory");
+        }
+      }
+    }
+  }
+}
+
+// Waits until every rank has published `epoch` into signals[0..world) (this rank's signal
+// array, written by the ranks' decode kernels), with a bounded spin: on timeout *status = 3.
+__global__ void wait_peers_kernel(const int* signals, int world, unsigned epoch, int* status) {
+  const int r = threadIdx.x;
+  if (r >= world) return;
+  for (long long i = 0; i < (1LL << 20); ++i) {
+    unsigned v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(signals + r) : "memory");
+    if (int(v - epoch) >= 0) return;
+    __nanosleep(256);
+  }
+  atomicExch(status, 3);
 }
 
 // --------------------------------------------------------------------------- host side
@@ -884,6 +944,13 @@ extern "C" int ts_paged_decode(void* out, const void* query, int64_t query_token
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   DecodeArgs a;
   a.out = out;
+  a.outs = nullptr;
+  a.n_out = 0;
+  a.out_row_stride = int64_t(num_q_heads) * head_dim;
+  a.out_head0 = 0;
+  a.signals = nullptr;
+  a.signal_index = 0;
+  a.epoch = 0;
   a.query = query;
   a.q_stride = query_token_stride;
   a.block_tables = block_tables;
@@ -1015,6 +1082,13 @@ extern "C" int ts_paged_decode_no_alloc(void* out, const void* query, int64_t qu
   uint8_t* ws = static_cast<uint8_t*>(scratch);
   DecodeArgs a;
   a.out = out;
+  a.outs = nullptr;
+  a.n_out = 0;
+  a.out_row_stride = int64_t(num_q_heads) * head_dim;
+  a.out_head0 = 0;
+  a.signals = nullptr;
+  a.signal_index = 0;
+  a.epoch = 0;
   a.query = query;
   a.q_stride = query_token_stride;
   a.block_tables = block_tables;
@@ -1044,4 +1118,174 @@ extern "C" int ts_paged_decode_no_alloc(void* out, const void* query, int64_t qu
   }
   TS_FAST_NA(__half)
 #undef TS_FAST_NA
+}
+
+// --------------------------------------------------------------------------- peer variant
+//
+// ts_paged_decode_peer: the decode of one rank of a KV-head-sharded model, fused with the
+// all-gather of the attention output. The rank's output rows go straight into every rank's
+// full output buffer (peer stores over NVLink, no staging copy and no collective kernel), and
+// the grid's last CTA publishes `epoch` into every rank's signal array; ts_wait_peers then
+// waits, on the device and with a bounded spin, until all ranks have done so.
+
+namespace {
+
+// Whether `p` is memory of the current device (the kernel dereferences these arrays).
+bool on_current_device(const void* p) {
+  cudaPointerAttributes attr{};
+  if (cudaPointerGetAttributes(&attr, p) != cudaSuccess) {
+    (void)cudaGetLastError();
+    return false;
+  }
+  int dev = -1;
+  return cudaGetDevice(&dev) == cudaSuccess && attr.type == cudaMemoryTypeDevice &&
+         attr.device == dev;
+}
+
+}  // namespace
+
+extern "C" int ts_paged_decode_peer(void* const* dst_outs, int32_t world, int32_t rank,
+                                    int32_t* const* signals, uint32_t epoch, const void* query,
+                                    int64_t query_token_stride, const void* key_pool,
+                                    const void* value_pool, const int32_t* block_tables,
+                                    int32_t max_blocks_per_seq, const int32_t* context_lens,
+                                    int32_t batch, int32_t num_q_heads, int32_t num_kv_heads,
+                                    int32_t head_dim, int32_t block_size, int64_t num_blocks,
+                                    float scale, int32_t dtype, void* workspace,
+                                    size_t workspace_bytes, void* stream) {
+  if (world < 1 || world > 64 || rank < 0 || rank >= world || epoch == 0)
+    return ts::set_error(TS_ERR_INVALID_ARGUMENT,
+                         "paged_decode_peer: bad world %d / rank %d / epoch %u", world, rank, epoch);
+  if (ts::dtype_size(dtype) == 0)
+    return ts::set_error(TS_ERR_INVALID_ARGUMENT, "paged_decode_peer: bad dtype %d", dtype);
+  if (batch < 0 || num_q_heads <= 0 || num_kv_heads <= 0 || num_q_heads % num_kv_heads ||
+      head_dim <= 0 || block_size <= 0 || num_blocks <= 0 || max_blocks_per_seq <= 0)
+    return ts::set_error(TS_ERR_INVALID_ARGUMENT, "paged_decode_peer: bad sizes");
+  if (query_token_stride < int64_t(num_q_heads) * head_dim)
+    return ts::set_error(TS_ERR_INVALID_ARGUMENT, "paged_decode_peer: query stride too small");
+  if (!dst_outs || !signals || !query || !key_pool || !value_pool || !block_tables ||
+      !context_lens)
+    return ts::set_error(TS_ERR_INVALID_ARGUMENT, "paged_decode_peer: null pointer");
+  if (!fast_path(num_q_heads, num_kv_heads, head_dim, block_size, dtype, num_blocks, key_pool,
+                 value_pool, query, query_token_stride, query))
+    return ts::set_error(TS_ERR_UNSUPPORTED,
+                         "paged_decode_peer: needs the tensor-core decode path (bf16/fp16, block "
+                         "16, head_dim 64/128, <= 16 query heads per KV head)");
+  if (!on_current_device(dst_outs) || !on_current_device(signals))
+    return ts::set_error(TS_ERR_INVALID_ARGUMENT,
+                         "paged_decode_peer: dst_outs and signals must be arrays in the memory of "
+                         "the current device");
+  if (batch > 8192 || int64_t(batch) * max_blocks_per_seq >= (int64_t(1) << 31) ||
+      max_blocks_per_seq > (1 << 20) || num_sms() * kWarps > kMaxGridWarps)
+    return ts::set_error(TS_ERR_UNSUPPORTED, "paged_decode_peer: sizes too large");
+  if (batch == 0) return ts::ok();
+  const int group = num_q_heads / num_kv_heads;
+  const int nt = group > 8 ? 2 : 1;
+  const WsLayout w =
+      ws_layout(batch, num_kv_heads, head_dim, max_blocks_per_seq, nt, num_sms() * kWarps);
+  if (workspace == nullptr || workspace_bytes < w.total)
+    return ts::set_error(TS_ERR_WORKSPACE_TOO_SMALL,
+                         "paged_decode_peer: workspace of %zu bytes, need %zu", workspace_bytes,
+                         w.total);
+  if (reinterpret_cast<uint64_t>(workspace) % 256)
+    return ts::set_error(TS_ERR_MISALIGNED, "paged_decode_peer: workspace not 256-byte aligned");
+  CUtensorMap km, vm;
+  const int64_t rows = num_blocks * num_kv_heads * kBlock;
+  if (!make_pool_map(&km, key_pool, rows, head_dim, dtype) ||
+      !make_pool_map(&vm, value_pool, rows, head_dim, dtype))
+    return ts::set_error(TS_ERR_INVALID_ARGUMENT, "paged_decode_peer: cannot encode TMA map of pool");
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  DecodeArgs a;
+  a.out = nullptr;
+  a.outs = dst_outs;
+  a.n_out = world;
+  a.out_row_stride = int64_t(world) * num_q_heads * head_dim;
+  a.out_head0 = rank * num_q_heads;
+  a.signals = reinterpret_cast<int* const*>(signals);
+  a.signal_index = rank;
+  a.epoch = epoch;
+  a.query = query;
+  a.q_stride = query_token_stride;
+  a.block_tables = block_tables;
+  a.context_lens = context_lens;
+  a.max_blocks = max_blocks_per_seq;
+  a.batch = batch;
+  a.num_q_heads = num_q_heads;
+  a.num_kv_heads = num_kv_heads;
+  a.group = group;
+  a.num_blocks = num_blocks;
+  a.scale_log2 = scale * kLog2e;
+  a.grid_warps = num_sms() * kWarps;
+  a.header = reinterpret_cast<int*>(ws);
+  a.chunk_prefix = reinterpret_cast<int*>(ws + w.chunk_prefix);
+  a.part_info = reinterpret_cast<int4*>(ws + w.part_info);
+  a.group_first = reinterpret_cast<int*>(ws + w.group_first);
+  a.arrive = reinterpret_cast<int*>(ws + w.arrive);
+  a.part_o = reinterpret_cast<float*>(ws + w.part_o);
+  a.part_ml = reinterpret_cast<float2*>(ws + w.part_ml);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+#define TS_FAST_PEER(T)                                                        \
+  if (head_dim == 128)                                                         \
+    return nt == 1 ? launch_fast<T, 128, 1>(a, km, vm, s)                      \
+                   : launch_fast<T, 128, 2>(a, km, vm, s);                     \
+  return nt == 1 ? launch_fast<T, 64, 1>(a, km, vm, s) : launch_fast<T, 64, 2>(a, km, vm, s);
+  if (dtype == TS_BFLOAT16) {
+    TS_FAST_PEER(__nv_bfloat16)
+  }
+  TS_FAST_PEER(__half)
+#undef TS_FAST_PEER
+}
+
+extern "C" int ts_wait_peers(const int32_t* local_signals, int32_t world, uint32_t epoch,
+                             int32_t* status, void* stream) {
+  if (world < 1 || world > 64 || epoch == 0 || !local_signals || !status)
+    return ts::set_error(TS_ERR_INVALID_ARGUMENT, "wait_peers: bad arguments");
+  wait_peers_kernel<<<1, 64, 0, static_cast<cudaStream_t>(stream)>>>(
+      reinterpret_cast<const int*>(local_signals), world, epoch, reinterpret_cast<int*>(status));
+  return ts::launch_status("wait_peers");
+}
+
+// Buffers shared between the ranks' processes: a plain device allocation (its own base, so its
+// IPC handle maps exactly it) and CUDA IPC handles to map a peer's.
+extern "C" int ts_peer_alloc(size_t bytes, void** ptr) {
+  if (bytes == 0 || ptr == nullptr)
+    return ts::set_error(TS_ERR_INVALID_ARGUMENT, "peer_alloc: bad arguments");
+  const cudaError_t e = cudaMalloc(ptr, bytes);
+  if (e != cudaSuccess)
+    return ts::set_error(static_cast<int>(e), "peer_alloc: %s", cudaGetErrorString(e));
+  return ts::ok();
+}
+
+extern "C" int ts_peer_free(void* ptr) {
+  const cudaError_t e = cudaFree(ptr);
+  if (e != cudaSuccess) return ts::set_error(static_cast<int>(e), "peer_free: %s", cudaGetErrorString(e));
+  return ts::ok();
+}
+
+extern "C" int ts_ipc_get_handle(const void* ptr, void* handle) {
+  if (ptr == nullptr || handle == nullptr)
+    return ts::set_error(TS_ERR_INVALID_ARGUMENT, "ipc_get_handle: null pointer");
+  cudaIpcMemHandle_t h;
+  const cudaError_t e = cudaIpcGetMemHandle(&h, const_cast<void*>(ptr));
+  if (e != cudaSuccess)
+    return ts::set_error(static_cast<int>(e), "ipc_get_handle: %s", cudaGetErrorString(e));
+  memcpy(handle, &h, sizeof(h));
+  return ts::ok();
+}
+
+extern "C" int ts_ipc_open(const void* handle, void** ptr) {
+  if (ptr == nullptr || handle == nullptr)
+    return ts::set_error(TS_ERR_INVALID_ARGUMENT, "ipc_open: null pointer");
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  const cudaError_t e = cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess)
+    return ts::set_error(static_cast<int>(e), "ipc_open: %s", cudaGetErrorString(e));
+  return ts::ok();
+}
+
+extern "C" int ts_ipc_close(void* ptr) {
+  const cudaError_t e = cudaIpcCloseMemHandle(ptr);
+  if (e != cudaSuccess) return ts::set_error(static_cast<int>(e), "ipc_close: %s", cudaGetErrorString(e));
+  return ts::ok();
 }

@@ -49,6 +49,17 @@ _SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "ts_swap_blocks": (
         ctypes.c_int, [_p, _i64, _i64, _p, _i64, _i64, _i64, _i64, _p, _i64, _p, _p]
     ),
+    "ts_paged_decode_peer": (
+        ctypes.c_int,
+        [_p, _i32, _i32, _p, ctypes.c_uint32, _p, _i64, _p, _p, _p, _i32, _p, _i32, _i32, _i32,
+         _i32, _i32, _i64, _f32, _i32, _p, ctypes.c_size_t, _p],
+    ),
+    "ts_wait_peers": (ctypes.c_int, [_p, _i32, ctypes.c_uint32, _p, _p]),
+    "ts_peer_alloc": (ctypes.c_int, [ctypes.c_size_t, ctypes.POINTER(ctypes.c_void_p)]),
+    "ts_peer_free": (ctypes.c_int, [_p]),
+    "ts_ipc_get_handle": (ctypes.c_int, [_p, _p]),
+    "ts_ipc_open": (ctypes.c_int, [_p, ctypes.POINTER(ctypes.c_void_p)]),
+    "ts_ipc_close": (ctypes.c_int, [_p]),
     "ts_add_rmsnorm": (ctypes.c_int, [_p, _p, _p, _p, _i64, _i32, _f32, _i32, _p]),
     "ts_rope_and_cache": (
         ctypes.c_int,
