@@ -62,6 +62,9 @@ def parse() -> argparse.Namespace:
     ap.add_argument("--collective", choices=["fused", "nccl"], default="fused",
                     help="decode70b at N>1: decode writing every rank's output buffer over "
                          "NVLink (fused) or decode + NCCL all-gather")  # fmt: skip
+    ap.add_argument("--resident-layers", type=int, default=0,
+                    help="decode70b: layer pools kept resident (0 = as many as fit); layers "
+                         "cycle through them, each still read in full from HBM")  # fmt: skip
     ap.add_argument("--shard-of", type=int, default=1,
                     help="decode70b on 1 GPU: run rank 0's share of an N-way KV-head split "
                          "(no collective), to measure the per-rank kernel alone")  # fmt: skip
@@ -584,6 +587,8 @@ def run_decode70b(args: argparse.Namespace, world: int, rank: int, local: int) -
     per_layer = 2 * nb * hkv_r * 16 * d * 2
     free, _ = torch.cuda.mem_get_info(dev)
     resident = max(1, min(layers, int(0.75 * free) // per_layer))
+    if args.resident_layers > 0:
+        resident = min(resident, args.resident_layers)
     g = torch.Generator(device=dev).manual_seed(3000 + rank)
     pools = torch.empty((resident, 2, nb, hkv_r, 16, d), dtype=dt, device=dev)
     for li in range(resident):
