@@ -218,6 +218,44 @@ def test_paged_decode_matches_oracle(cuda_device, dtype, hq, hkv, head_dim) -> N
         assert_attention_close(out, ref, dtype)
 
 
+@pytest.mark.parametrize(
+    ("batch", "lo", "hi", "mode"),
+    [
+        (24, 16, 2000, 0),  # few blocks per warp: static even split
+        (64, 2500, 4200, 1),  # ~12k blocks x 8 heads: dynamic claiming, 32-block items
+        (104, 2000, 2300, 1),  # ~14k blocks x 8 heads: dynamic claiming, 64-block items
+    ],
+)
+def test_paged_decode_schedules_match_oracle(cuda_device, batch, lo, hi, mode) -> None:  # type: ignore[no-untyped-def]
+    """Both schedules of the prep kernel (static split below 80 blocks per warp, dynamic
+    claiming above) at the Llama-3-8B geometry, one empty context among the sequences; the
+    chosen schedule is read back from the workspace header, and a second call on the reused
+    workspace is bit-identical (fixed merge order)."""
+    rng = np.random.default_rng(batch)
+    ctx = [int(c) for c in rng.integers(lo, hi, batch)]
+    ctx[batch // 2] = 0
+    hq, hkv, d, dtype = 32, 8, 128, torch.bfloat16
+    case = small_paged_case(batch, ctx, num_q_heads=hq, num_kv_heads=hkv, head_dim=d)
+    k, v, dk, dv = make_pools(case, dtype, cuda_device)
+    q = (torch.randn(case.batch, hq, d, generator=torch.Generator().manual_seed(3)) * 0.5).to(dtype)
+    ref = oatt.paged_decode_np(q.float().numpy(), k.float().numpy(), v.float().numpy(),
+                               case.block_tables, case.context_lens, d**-0.5)  # fmt: skip
+    bt = torch.from_numpy(case.block_tables).to(cuda_device)
+    cl = torch.from_numpy(case.context_lens).to(cuda_device)
+    ws = torch.empty(ops.decode_workspace_size(case.batch, hq, hkv, d, bt.shape[1], 16, dtype),
+                     dtype=torch.uint8, device=cuda_device)  # fmt: skip
+    outs = []
+    for _ in range(2):
+        out = torch.full((case.batch, hq, d), 9.0, dtype=dtype, device=cuda_device)
+        ops.paged_decode(out, q.to(cuda_device), dk, dv, bt, cl, d**-0.5, ws)
+        torch.cuda.synchronize()
+        outs.append(out)
+    assert int(ws[8:12].view(torch.int32)) == mode  # header[2]: 1 = dynamic claiming
+    assert torch.equal(outs[0], outs[1])
+    assert not outs[0][batch // 2].any()
+    assert_attention_close(outs[0], ref, dtype)
+
+
 def test_paged_decode_strided_query_and_empty_context(cuda_device) -> None:  # type: ignore[no-untyped-def]
     dtype, hq, hkv, d = torch.bfloat16, 32, 8, 128
     case = small_paged_case(4, [0, 40, 300], num_q_heads=hq, num_kv_heads=hkv, head_dim=d)
