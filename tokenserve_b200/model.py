@@ -213,11 +213,12 @@ class PagedLlamaRunner:
         return out
 
     @torch.inference_mode()
-    def forward(self, st: DeviceStep) -> torch.Tensor:
-        """Runs every layer over the step's tokens; returns float32 logits of the sampled rows."""
-        if self.fused and self.tag_pool is None:
-            return self._forward_fused(st)
-        return self._forward_modules(st)
+    def forward(self, st: DeviceStep, float_logits: bool = True) -> torch.Tensor:
+        """Runs every layer over the step's tokens; returns the logits of the sampled rows, in
+        float32 or (``float_logits=False``) in the model dtype."""
+        logits = self._forward_fused(st) if self.fused and self.tag_pool is None else (
+            self._forward_modules(st))  # fmt: skip
+        return logits.float() if float_logits else logits
 
     def _forward_fused(self, st: DeviceStep) -> torch.Tensor:
         """Per layer: add+RMSNorm, QKV GEMM, RoPE+K1, K2/K3, O GEMM, add+RMSNorm, gate-up GEMM,
@@ -248,7 +249,7 @@ class PagedLlamaRunner:
                                 self._eps[li + 1][0])  # fmt: skip
             else:
                 ops.add_rmsnorm(x, res, mo, self.base.norm.weight, self.base.norm.variance_epsilon)
-        return self.model.lm_head(x[st.sample_rows]).float()
+        return self.model.lm_head(x[st.sample_rows])
 
     def _forward_modules(self, st: DeviceStep) -> torch.Tensor:
         h = self.base.embed_tokens(st.input_ids)
@@ -266,7 +267,7 @@ class PagedLlamaRunner:
             h = h + attn.o_proj(o.view(t, hq * d))
             h = h + layer.mlp(layer.post_attention_layernorm(h))
         hs = self.base.norm(h[st.sample_rows])
-        return self.model.lm_head(hs).float()
+        return self.model.lm_head(hs)
 
 
 def _bucket(n: int, step: int) -> int:
@@ -341,7 +342,9 @@ class DecodeGraphs:
             graph = torch.cuda.CUDAGraph()
             with torch.cuda.graph(graph):
                 torch.index_select(self.tables[:, :w], 0, rows, out=dtab)
-                logits = r.forward(st)
+                # Logits stay in the model dtype: the argmax is the same, and the (rare)
+                # temperature sampling converts its own row.
+                logits = r.forward(st, float_logits=False)
                 tokens = torch.argmax(logits, dim=-1)
         finally:
             r._ws = saved
