@@ -44,6 +44,15 @@ namespace {
 #ifndef TS_DECODE_STAGES_D128
 #define TS_DECODE_STAGES_D128 3  // ring stages per warp at head_dim 128
 #endif
+#ifndef TS_DECODE_MIN_ITEMS_PER_WARP
+#define TS_DECODE_MIN_ITEMS_PER_WARP 2  // dynamic claiming: the item size gives every warp this many
+#endif
+#ifndef TS_DECODE_PREFETCH_BLOCKS
+#define TS_DECODE_PREFETCH_BLOCKS 4  // the next item is fetched this many blocks before the end
+#endif
+#ifndef TS_DECODE_HEAVY_PARTS
+#define TS_DECODE_HEAVY_PARTS 4  // dynamic claiming: sequences with this many partitions go first (0: none)
+#endif
 #ifndef TS_DECODE_ONE_BOX
 #define TS_DECODE_ONE_BOX 0  // 1: one 4 KiB TMA box per 128-dim tile instead of two 2 KiB
 #endif
@@ -66,6 +75,8 @@ constexpr int kBlock = 16;                          // tokens per KV block
 constexpr int kPartBlocks = TS_DECODE_PART_BLOCKS;
 constexpr int kMinPartBlocks = 16;
 constexpr int kStaticMaxBlocksPerWarp = TS_DECODE_STATIC_MAX_BLOCKS;
+constexpr int kMinItemsPerWarp = TS_DECODE_MIN_ITEMS_PER_WARP;
+constexpr int kHeavyParts = TS_DECODE_HEAVY_PARTS;
 static_assert(kPartBlocks >= 2 && kPartBlocks <= 64, "a work item's table fits two registers per lane");
 // Upper bound of the grid's warps (SMs x warps per CTA), used to size the workspace.
 constexpr int kMaxGridWarps = 8192;
@@ -247,61 +258,81 @@ __device__ void prep_static(DecodeArgs& a, int* warp_sums, long long WB, int run
 }
 
 // Dynamic claiming (large steps): partitions of pb blocks of every (sequence, head), pb the
-// largest of 64 / 32 / 16 that gives every warp two; full partitions first and the partial last
-// ones longest first (counting sort), so the kernel's tail is made of the shortest items.
+// largest of 64 / 32 / 16 that gives every warp kMinItemsPerWarp. Claim order, by counting sort:
+//   1. every partition of the sequences with at least kHeavyParts partitions, sequence by
+//      sequence, most partitions first — their merges (the last warp to finish one of them reads
+//      all its partials) then run while the other warps still stream, not in the kernel's tail;
+//   2. the full partitions of the other sequences;
+//   3. the remaining partial partitions, longest first, so the tail is made of the shortest items.
+// The order only decides which warp runs a partition; every partition's partial result and
+// every merge (fixed partition order) are the same whatever the order, so outputs are too.
+constexpr int kPartsCap = 512;  // sequences with more partitions share the first bucket
+constexpr int kClassFull = kPartsCap + 1;
+constexpr int kSortBuckets = kClassFull + 1 + kPartBlocks;
+
 __device__ void prep_dynamic(DecodeArgs& a, int* warp_sums, int cnt, int b0) {
-  __shared__ int hist[kPartBlocks], cursor[kPartBlocks];
+  static_assert(kSortBuckets <= kPrepThreads, "one sort bucket per prep thread");
+  __shared__ int bucket[kSortBuckets];  // counts, then cursors
   const int B = a.batch, H = a.num_kv_heads;
-  if (threadIdx.x < kPartBlocks) hist[threadIdx.x] = 0;
-  // pb: the largest candidate with two items per warp; its partition scan is kept.
+  for (int i = threadIdx.x; i < kSortBuckets; i += blockDim.x) bucket[i] = 0;
+  // pb: the largest candidate with kMinItemsPerWarp items per warp; its partition scan is kept.
   int pb = kMinPartBlocks, run_p = 0, total_parts = 0;
   for (int cand = kPartBlocks; cand >= kMinPartBlocks; cand /= 2) {
     int n = 0;
     for (int i = 0; i < cnt; ++i) n += (blocks_of(ctx_of(a, b0 + i)) + cand - 1) / cand;
     int total = 0;
     const int run = block_exclusive_scan(n, &total, warp_sums);
-    if (cand == kMinPartBlocks || int64_t(total) * H >= 2 * int64_t(a.grid_warps)) {
+    if (cand == kMinPartBlocks || int64_t(total) * H >= kMinItemsPerWarp * int64_t(a.grid_warps)) {
       pb = cand;
       run_p = run;
       total_parts = total;
       break;
     }
   }
-  int full = 0;
-  for (int i = 0; i < cnt; ++i) full += blocks_of(ctx_of(a, b0 + i)) / pb;
-  int total_full = 0;
-  int run_f = block_exclusive_scan(full, &total_full, warp_sums);
+  // Bucket of a sequence of n blocks (np partitions): heavy ones by partition count, descending;
+  // the full partitions of the others in one bucket; their partial partitions by size, descending.
+  auto heavy = [&](int np) { return kHeavyParts > 0 && np >= kHeavyParts; };
+  auto heavy_bucket = [&](int np) { return kPartsCap - min(np, kPartsCap); };
+  auto partial_bucket = [&](int n) { return kClassFull + 1 + (pb - n % pb); };
+  for (int i = 0; i < cnt; ++i) {
+    const int n = blocks_of(ctx_of(a, b0 + i)), np = (n + pb - 1) / pb;
+    if (heavy(np)) {
+      atomicAdd(&bucket[heavy_bucket(np)], np);
+    } else {
+      if (n / pb) atomicAdd(&bucket[kClassFull], n / pb);
+      if (n % pb) atomicAdd(&bucket[partial_bucket(n)], 1);
+    }
+  }
+  __syncthreads();
+  int sorted = 0;
+  const int first = block_exclusive_scan(
+      threadIdx.x < kSortBuckets ? bucket[threadIdx.x] : 0, &sorted, warp_sums);
+  if (threadIdx.x < kSortBuckets) bucket[threadIdx.x] = first;  // every count was read above
+  __syncthreads();
   // Partition p of sequence b -> claim position q (items q * H + h, one per head).
   auto put = [&](int q, int b, int p, int n, int c0, int ctx) {
     a.part_info[2 * q] = make_int4(b, p * pb, min(pb, n - p * pb), p);
     a.part_info[2 * q + 1] = make_int4(c0, (n + pb - 1) / pb, ctx, 0);
   };
-  const int run_p0 = run_p;
   for (int i = 0; i < cnt; ++i) {
-    const int b = b0 + i, ctx = ctx_of(a, b), n = blocks_of(ctx);
+    const int b = b0 + i, ctx = ctx_of(a, b), n = blocks_of(ctx), np = (n + pb - 1) / pb;
     a.chunk_prefix[b] = run_p;
-    for (int p = 0; p < n / pb; ++p) put(run_f + p, b, p, n, run_p, ctx);
-    if (n % pb) atomicAdd(&hist[n % pb], 1);
-    run_p += (n + pb - 1) / pb;
-    run_f += n / pb;
-  }
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    int off = total_full;
-    for (int sz = pb - 1; sz >= 1; --sz) {  // longest partial partitions first
-      cursor[sz] = off;
-      off += hist[sz];
+    if (heavy(np)) {
+      const int q = atomicAdd(&bucket[heavy_bucket(np)], np);
+      for (int p = 0; p < np; ++p) put(q + p, b, p, n, run_p, ctx);
+    } else {
+      if (n / pb) {
+        const int q = atomicAdd(&bucket[kClassFull], n / pb);
+        for (int p = 0; p < n / pb; ++p) put(q + p, b, p, n, run_p, ctx);
+      }
+      if (n % pb) put(atomicAdd(&bucket[partial_bucket(n)], 1), b, n / pb, n, run_p, ctx);
     }
+    run_p += np;
+  }
+  if (threadIdx.x == 0) {
     a.chunk_prefix[B] = total_parts;
     a.header[2] = 1;
     a.header[3] = total_parts * H;
-  }
-  __syncthreads();
-  int c0 = run_p0;
-  for (int i = 0; i < cnt; ++i) {
-    const int ctx = ctx_of(a, b0 + i), n = blocks_of(ctx);
-    if (n % pb) put(atomicAdd(&cursor[n % pb], 1), b0 + i, n / pb, n, c0, ctx);
-    c0 += (n + pb - 1) / pb;
   }
 }
 
@@ -394,21 +425,6 @@ struct ItemInfo {
   int b, h, blk0, nparts, ctx, nblk, part_global, slot0;
 };
 
-// (Partition, KV head) -> blocks to read and the partial-result slots of its (sequence, head).
-__device__ __forceinline__ ItemInfo decode_item(const DecodeArgs& a, int part, int h) {
-  ItemInfo it;
-  const int4 d = __ldg(a.part_info + 2 * part), e = __ldg(a.part_info + 2 * part + 1);
-  it.b = d.x;
-  it.h = h;
-  it.blk0 = d.y;
-  it.nblk = d.z;
-  it.nparts = e.y;
-  it.slot0 = e.x * a.num_kv_heads + h * it.nparts;
-  it.part_global = it.slot0 + d.w;
-  it.ctx = e.z;
-  return it;
-}
-
 template <typename T, int D, int NT>
 __global__ void __launch_bounds__(kWarps * 32, 1)
     paged_decode_kernel(const __grid_constant__ CUtensorMap kmap,
@@ -447,42 +463,87 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
   int nxt = 0, part_end = 0, my_h = 0;
   if (dynamic) {
     part_end = __ldg(a.header + 3);
-    int c = 0;
-    if (lane == 0) c = atomicAdd(a.header, 1);
-    nxt = __shfl_sync(0xffffffffu, c, 0);
   } else if (gw / H < __ldg(a.header + 3)) {
     my_h = gw % H;
     nxt = __ldg(a.group_first + gw / H);
     part_end = __ldg(a.group_first + gw / H + 1);
   }
 
-  // ---- producer state (warp-uniform except p_table, one table entry per lane)
+  // ---- producer state (warp-uniform except the tables, one table entry per lane)
   constexpr int TABW = (kPartBlocks + 31) / 32;  // table entries per lane
   int p_item = -1, p_blk = 0, p_nblk = 0;
   ItemInfo p_it{};
   int p_table[TABW];
   bool p_done = false;
 
+  // The next item is fetched by a chain of dependent loads (claim counter, descriptor, table
+  // row), advanced one step per produce() call once at most kPrefetchBlocks blocks of the
+  // current item remain to be issued: the latencies hide behind the current item's last
+  // blocks, and a dynamic claim is made only shortly before the warp can start it, so no warp
+  // holds a claimed item while other warps run out of work.
+  constexpr int kPrefetchBlocks = TS_DECODE_PREFETCH_BLOCKS;
+  int f_state = 0;  // 0 idle, 1 claim issued, 2 descriptor loads issued, 3 ready, -1 no more work
+  int f_claim = 0, f_h = 0, f_item = 0;
+  int4 f_d = make_int4(0, 0, 0, 0), f_e = make_int4(0, 0, 0, 0);
+  ItemInfo f_it{};
+  int f_table[TABW];
+  auto issue_descriptor = [&](int part, int h, int item) {
+    f_h = h;
+    f_item = item;
+    f_d = __ldg(a.part_info + 2 * part);
+    f_e = __ldg(a.part_info + 2 * part + 1);
+    f_state = 2;
+  };
+  auto fetch_step = [&]() {
+    if (f_state == 0) {
+      if (dynamic) {
+        if (lane == 0) f_claim = atomicAdd(a.header, 1);
+        f_state = 1;
+      } else if (nxt < part_end) {
+        issue_descriptor(nxt, my_h, nxt * H + my_h);
+        ++nxt;
+      } else {
+        f_state = -1;
+      }
+    } else if (f_state == 1) {
+      const int c = __shfl_sync(0xffffffffu, f_claim, 0);
+      if (c < part_end) {
+        issue_descriptor(c / H, c % H, c);
+      } else {
+        f_state = -1;
+      }
+    } else if (f_state == 2) {
+      // (partition, KV head) -> blocks to read and the partial-result slots of its
+      // (sequence, head)
+      f_it.b = f_d.x;
+      f_it.h = f_h;
+      f_it.blk0 = f_d.y;
+      f_it.nblk = f_d.z;
+      f_it.nparts = f_e.y;
+      f_it.slot0 = f_e.x * a.num_kv_heads + f_h * f_it.nparts;
+      f_it.part_global = f_it.slot0 + f_d.w;
+      f_it.ctx = f_e.z;
+      const int32_t* row = a.block_tables + int64_t(f_it.b) * a.max_blocks + f_it.blk0;
+#pragma unroll
+      for (int w = 0; w < TABW; ++w)
+        f_table[w] = lane + 32 * w < f_it.nblk ? __ldg(row + lane + 32 * w) : 0;
+      f_state = 3;
+    }
+  };
+
   auto produce = [&](int s) {
     if (!p_done && p_blk == p_nblk) {
-      if (nxt < part_end) {
-        p_it = dynamic ? decode_item(a, nxt / H, nxt % H) : decode_item(a, nxt, my_h);
-        p_item = dynamic ? nxt : nxt * H + my_h;
-        if (dynamic) {
-          int c = 0;
-          if (lane == 0) c = atomicAdd(a.header, 1);
-          nxt = __shfl_sync(0xffffffffu, c, 0);
-        } else {
-          ++nxt;
-        }
+      while (f_state >= 0 && f_state < 3) fetch_step();  // first item, or a short one
+      if (f_state < 0) {
+        p_done = true;
+      } else {
+        p_it = f_it;
+        p_item = f_item;
+#pragma unroll
+        for (int w = 0; w < TABW; ++w) p_table[w] = f_table[w];
         p_nblk = p_it.nblk;
         p_blk = 0;
-        const int32_t* row = a.block_tables + int64_t(p_it.b) * a.max_blocks + p_it.blk0;
-#pragma unroll
-        for (int w = 0; w < TABW; ++w)
-          p_table[w] = lane + 32 * w < p_it.nblk ? __ldg(row + lane + 32 * w) : 0;
-      } else {
-        p_done = true;
+        f_state = 0;
       }
     }
     if (p_done) {
@@ -519,6 +580,7 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
       }
     }
     ++p_blk;
+    if (f_state >= 0 && f_state < 3 && p_nblk - p_blk <= kPrefetchBlocks) fetch_step();
   };
 
 #pragma unroll 1
@@ -621,19 +683,58 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
     if (lane == 0) old = atomicAdd(a.arrive + it.b * a.num_kv_heads + it.h, 1);
     old = __shfl_sync(0xffffffffu, old, 0);
     if (old != it.nparts - 1) return;
-    // Last partition of (b, h) to finish: merge all of them.
     __threadfence();
+    // Last partition of (b, h) to finish: merge all of them. A long sequence has tens of
+    // partitions and its merge can run in the kernel's tail, so the loads of several
+    // partitions are kept in flight at once (the sums still run in partition order).
     const int hd = lane % NT8;  // fixed head per lane in the [D][NT8] layout
     const int64_t slot0 = it.slot0;
+    const int np = it.nparts;
+    // Running max: the lanes of one head split the partitions (32 / NT8 per pass, four passes'
+    // loads in flight), then reduce across those lanes.
+    constexpr int kLanesPerHead = 32 / NT8;
     float mx = -INFINITY;
-    for (int p = 0; p < it.nparts; ++p)
-      mx = fmaxf(mx, __ldcg(&a.part_ml[(slot0 + p) * NT8 + hd].x));
+    for (int p0 = lane / NT8; p0 < np; p0 += 4 * kLanesPerHead) {
+      float v[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int p = p0 + u * kLanesPerHead;
+        v[u] = p < np ? __ldcg(&a.part_ml[(slot0 + p) * NT8 + hd].x) : -INFINITY;
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) mx = fmaxf(mx, v[u]);
+    }
+#pragma unroll
+    for (int o = NT8; o < 32; o <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
     constexpr int PER = D * NT8 / 32;
     float acc[PER];
 #pragma unroll
     for (int i = 0; i < PER; ++i) acc[i] = 0.f;
     float lsum = 0.f;
-    for (int p = 0; p < it.nparts; ++p) {
+    int p = 0;
+    for (; p + 1 < np; p += 2) {  // two partitions' loads in flight
+      const int64_t s0 = slot0 + p, s1 = s0 + 1;
+      const float2 ml0 = __ldcg(&a.part_ml[s0 * NT8 + hd]);
+      const float2 ml1 = __ldcg(&a.part_ml[s1 * NT8 + hd]);
+      const float* src0 = a.part_o + s0 * D * NT8;
+      const float* src1 = a.part_o + s1 * D * NT8;
+      float x0[PER], x1[PER];
+#pragma unroll
+      for (int i = 0; i < PER; ++i) {
+        x0[i] = __ldcg(src0 + lane + 32 * i);
+        x1[i] = __ldcg(src1 + lane + 32 * i);
+      }
+      const float w0 = ml0.x == -INFINITY ? 0.f : exp2f(ml0.x - mx);
+      const float w1 = ml1.x == -INFINITY ? 0.f : exp2f(ml1.x - mx);
+      lsum += w0 * ml0.y;
+      lsum += w1 * ml1.y;
+#pragma unroll
+      for (int i = 0; i < PER; ++i) {
+        acc[i] += w0 * x0[i];
+        acc[i] += w1 * x1[i];
+      }
+    }
+    if (p < np) {
       const int64_t sl = slot0 + p;
       const float2 ml = __ldcg(&a.part_ml[sl * NT8 + hd]);
       const float w = ml.x == -INFINITY ? 0.f : exp2f(ml.x - mx);
