@@ -630,7 +630,7 @@ def run_decode70b(args: argparse.Namespace, world: int, rank: int, local: int) -
             if fused:
                 # K2 writes this rank's heads into every rank's buffer p over NVLink; the wait
                 # (a one-block kernel on this stream) holds later work until all ranks have.
-                epoch = pg.decode(p, q, pool[0], pool[1], bt, cl, d**-0.5, ws)
+                epoch = pg.decode(p, q, pool[0], pool[1], bt, cl, d**-0.5, ws, reuse_plan=li > 0)
                 if dec_ev is not None:
                     dec_ev[li][1].record(comp)
                     ag_ev[li][0].record(comp)
@@ -638,7 +638,7 @@ def run_decode70b(args: argparse.Namespace, world: int, rank: int, local: int) -
                 if ag_ev is not None:
                     ag_ev[li][1].record(comp)
                 continue
-            ops.paged_decode(outs[p], q, pool[0], pool[1], bt, cl, d**-0.5, ws)
+            ops.paged_decode(outs[p], q, pool[0], pool[1], bt, cl, d**-0.5, ws, reuse_plan=li > 0)
             if dec_ev is not None:
                 dec_ev[li][1].record(comp)
             if world > 1:
@@ -732,7 +732,8 @@ def run_decode70b(args: argparse.Namespace, world: int, rank: int, local: int) -
                           if fused else
                           {"bytes_per_layer": ag_bytes, "avg_us": round(ag_t * 1e6, 2),
                            "algbw_gbs": round(ag_bytes / ag_t / 1e9, 1)}),
-            "gpu_launches": ((4 if fused else 3 + (2 if world > 1 else 0)) * layers) * args.steps,
+            # per layer K1 + decode (+ the peer wait), and one prep kernel per step (layer 0)
+            "gpu_launches": (((3 if fused else 2 + (2 if world > 1 else 0)) * layers) + 1) * args.steps,
             "clocks": clocks.summary(),
         }  # fmt: skip
         print(json.dumps(line), flush=True)

@@ -110,6 +110,29 @@ int ts_paged_decode(void* out, const void* query, int64_t query_token_stride,
                     int32_t block_size, int64_t num_blocks, float scale, int32_t dtype,
                     void* workspace, size_t workspace_bytes, void* stream);
 
+/*
+ * K2 that reuses the work plan an earlier ts_paged_decode left in `workspace` (a model's later
+ * layers in one decode step: every layer has the same block tables and context lengths).
+ *
+ * Replaces: the same eager attention as ts_paged_decode (one call per layer in
+ * src/tokenserve/backends/hf.py:71); the plan reuse itself has no counterpart in the reference.
+ * ts_paged_decode runs a one-CTA prep kernel (partition descriptors, claim order, prefix sums)
+ * before the decode kernel; this call launches the decode kernel alone. Arguments as
+ * ts_paged_decode. Preconditions: the earlier call, ordered before this one on the GPU, used
+ * the same workspace, block_tables contents, context_lens contents, batch, num_kv_heads and
+ * max_blocks_per_seq, and took the tensor-core path (same dtype, head_dim, block_size and
+ * pointer alignment as here). A plan made for another batch, head count, table width or grid
+ * is detected on the device: nothing is written and the workspace's status word (int32 at
+ * byte 4) is set to 4. Changed table or length contents are not detected.
+ */
+int ts_paged_decode_planned(void* out, const void* query, int64_t query_token_stride,
+                            const void* key_pool, const void* value_pool,
+                            const int32_t* block_tables, int32_t max_blocks_per_seq,
+                            const int32_t* context_lens, int32_t batch, int32_t num_q_heads,
+                            int32_t num_kv_heads, int32_t head_dim, int32_t block_size,
+                            int64_t num_blocks, float scale, int32_t dtype, void* workspace,
+                            size_t workspace_bytes, void* stream);
+
 /* Size of the device scratch built into the library for ts_paged_decode_no_alloc (32 MiB). */
 #define TS_NO_ALLOC_SCRATCH_BYTES (32u << 20)
 
@@ -235,6 +258,8 @@ int ts_verify_tags(const int32_t* tag_pool, const int32_t* block_tables,
  * CTA then writes `epoch` (non-zero, increasing per call) into signals[r][rank] for every r.
  * dst_outs and signals are device arrays of device pointers (peer buffers mapped with
  * ts_ipc_open); the tensor-core decode path is required (TS_ERR_UNSUPPORTED otherwise).
+ * reuse_plan = 1 skips the prep kernel and runs the plan an earlier call left in `workspace`,
+ * under the preconditions of ts_paged_decode_planned.
  */
 int ts_paged_decode_peer(void* const* dst_outs, int32_t world, int32_t rank,
                          int32_t* const* signals, uint32_t epoch, const void* query,
@@ -243,7 +268,7 @@ int ts_paged_decode_peer(void* const* dst_outs, int32_t world, int32_t rank,
                          const int32_t* context_lens, int32_t batch, int32_t num_q_heads,
                          int32_t num_kv_heads, int32_t head_dim, int32_t block_size,
                          int64_t num_blocks, float scale, int32_t dtype, void* workspace,
-                         size_t workspace_bytes, void* stream);
+                         size_t workspace_bytes, int32_t reuse_plan, void* stream);
 
 /*
  * Waits on the device until local_signals[r] >= epoch for every r < world (every rank's

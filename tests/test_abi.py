@@ -30,7 +30,8 @@ def declared() -> list[str]:
 
 def test_header_declares_the_entry_points() -> None:
     names = declared()
-    for want in ("ts_reshape_and_cache", "ts_paged_decode", "ts_paged_prefill",
+    for want in ("ts_reshape_and_cache", "ts_paged_decode", "ts_paged_decode_planned",
+                 "ts_paged_prefill",
                  "ts_copy_blocks", "ts_version", "ts_last_error", "ts_verify_tags",
                  "ts_paged_decode_workspace_size", "ts_swap_blocks", "ts_add_rmsnorm",
                  "ts_rope_and_cache", "ts_silu_mul"):  # fmt: skip
@@ -69,6 +70,9 @@ def test_argument_errors_are_reported_before_any_launch(lib: ctypes.CDLL) -> Non
     rc = lib.ts_paged_decode(None, None, 4096, None, None, None, 8, None, 2, 30, 8, 128, 16,
                              100, 0.1, ops.TS_BFLOAT16, None, 0, None)  # fmt: skip
     assert rc == -1 and b"bad sizes" in lib.ts_last_error()
+    rc = lib.ts_paged_decode_planned(None, None, 4096, None, None, None, 8, None, 2, 30, 8, 128,
+                                     16, 100, 0.1, ops.TS_BFLOAT16, None, 0, None)  # fmt: skip
+    assert rc == -1 and b"bad sizes" in lib.ts_last_error()
     rc = lib.ts_copy_blocks(None, 2, 10, 100, 1, None, 1, None, None)
     assert rc == -1 and b"copy_blocks" in lib.ts_last_error()
     rc = lib.ts_swap_blocks(None, 10, 100, None, 4096, 4, 2, 64, None, 1, None, None)
@@ -77,10 +81,10 @@ def test_argument_errors_are_reported_before_any_launch(lib: ctypes.CDLL) -> Non
     assert rc == -1 and b"null pointer" in lib.ts_last_error()
     assert lib.ts_swap_blocks(None, 6400, 100, None, 256, 4, 2, 64, None, 0, None, None) == 0
     rc = lib.ts_paged_decode_peer(None, 0, 0, None, 1, None, 4096, None, None, None, 8, None, 2,
-                                  32, 8, 128, 16, 100, 0.1, ops.TS_BFLOAT16, None, 0, None)  # fmt: skip
+                                  32, 8, 128, 16, 100, 0.1, ops.TS_BFLOAT16, None, 0, 0, None)  # fmt: skip
     assert rc == -1 and b"paged_decode_peer: bad world" in lib.ts_last_error()
     rc = lib.ts_paged_decode_peer(None, 2, 0, None, 0, None, 4096, None, None, None, 8, None, 2,
-                                  32, 8, 128, 16, 100, 0.1, ops.TS_BFLOAT16, None, 0, None)  # fmt: skip
+                                  32, 8, 128, 16, 100, 0.1, ops.TS_BFLOAT16, None, 0, 0, None)  # fmt: skip
     assert rc == -1 and b"epoch" in lib.ts_last_error()
     assert lib.ts_wait_peers(None, 2, 1, None, None) == -1
     # Empty work is a successful no-op and clears the message.

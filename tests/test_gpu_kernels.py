@@ -256,6 +256,45 @@ def test_paged_decode_schedules_match_oracle(cuda_device, batch, lo, hi, mode) -
     assert_attention_close(outs[0], ref, dtype)
 
 
+@pytest.mark.parametrize(("batch", "lo", "hi", "mode"), [(24, 16, 2000, 0), (104, 2000, 2300, 1)])
+def test_paged_decode_reuses_the_plan_across_layers(cuda_device, batch, lo, hi, mode) -> None:  # type: ignore[no-untyped-def]
+    """Layer 0 of a step plans and runs (ts_paged_decode); layers 1-3 run the same plan
+    (ts_paged_decode_planned) on their own pools, queries and outputs. Each layer's output is
+    bit-identical to a call that plans from scratch, the empty context's rows are zeros, and the
+    kernel leaves the claim counter at zero. A plan made for another batch is refused on the
+    device: status 4, nothing written."""
+    rng = np.random.default_rng(batch + 7)
+    ctx = [int(c) for c in rng.integers(lo, hi, batch)]
+    ctx[batch // 3] = 0
+    hq, hkv, d, dtype = 32, 8, 128, torch.bfloat16
+    case = small_paged_case(batch, ctx, num_q_heads=hq, num_kv_heads=hkv, head_dim=d)
+    bt = torch.from_numpy(case.block_tables).to(cuda_device)
+    cl = torch.from_numpy(case.context_lens).to(cuda_device)
+    n = ops.decode_workspace_size(case.batch, hq, hkv, d, bt.shape[1], 16, dtype)
+    ws = torch.empty(n, dtype=torch.uint8, device=cuda_device)
+    ws_fresh = torch.empty(n, dtype=torch.uint8, device=cuda_device)
+    for layer in range(4):
+        _, _, dk, dv = make_pools(case, dtype, cuda_device, seed=20 + layer)
+        q = (torch.randn(case.batch, hq, d, generator=torch.Generator().manual_seed(layer)) * 0.5)
+        q = q.to(dtype).to(cuda_device)
+        out = torch.full((case.batch, hq, d), 9.0, dtype=dtype, device=cuda_device)
+        ref = torch.full_like(out, 5.0)
+        ops.paged_decode(out, q, dk, dv, bt, cl, d**-0.5, ws, reuse_plan=layer > 0)
+        ops.paged_decode(ref, q, dk, dv, bt, cl, d**-0.5, ws_fresh)
+        torch.cuda.synchronize()
+        assert torch.equal(out, ref), f"layer {layer}"
+        assert not out[batch // 3].any()
+        header = ws[:40].view(torch.int32).tolist()
+        assert header[0] == 0 and header[1] == 0 and header[2] == mode and header[4] == 0
+    # A plan for this batch does not fit a call with one sequence fewer.
+    out = torch.full((case.batch - 1, hq, d), 3.0, dtype=dtype, device=cuda_device)
+    ops.paged_decode(out, q[:-1], dk, dv, bt[:-1].contiguous(), cl[:-1].contiguous(), d**-0.5,
+                     ws, reuse_plan=True)  # fmt: skip
+    torch.cuda.synchronize()
+    assert int(ws[4:8].view(torch.int32)) == 4
+    assert bool((out == 3.0).all())
+
+
 def test_paged_decode_strided_query_and_empty_context(cuda_device) -> None:  # type: ignore[no-untyped-def]
     dtype, hq, hkv, d = torch.bfloat16, 32, 8, 128
     case = small_paged_case(4, [0, 40, 300], num_q_heads=hq, num_kv_heads=hkv, head_dim=d)

@@ -33,7 +33,7 @@ def _peer_call(lib, dst, world, rank, sig, epoch, q, kp, vp, bt, cl, scale, ws):
         dst.data_ptr(), world, rank, sig.data_ptr(), epoch, q.data_ptr(), q.stride(0),
         kp.data_ptr(), vp.data_ptr(), bt.data_ptr(), bt.shape[1], cl.data_ptr(), q.shape[0],
         q.shape[1], hkv, d, bs, nb, scale, ops.TS_BFLOAT16, ws.data_ptr(),
-        ws.numel(), torch.cuda.current_stream().cuda_stream,
+        ws.numel(), 0, torch.cuda.current_stream().cuda_stream,
     )  # fmt: skip
     assert code == 0, lib.ts_last_error()
 

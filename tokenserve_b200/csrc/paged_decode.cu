@@ -108,8 +108,11 @@ struct DecodeArgs {
   int64_t num_blocks;
   float scale_log2;
   // [0] claim counter, [1] status, [2] 1 = dynamic claiming, [3] items to claim (dynamic) or
-  // groups (static), [4] CTAs finished (completion signal)
+  // groups (static), [4] CTAs finished, [6..9] the plan's batch, KV heads, table width and grid
+  // warps. The main kernel's last CTA re-zeroes [0] and [4], so a later launch can run the
+  // same plan (block tables and context lengths unchanged) without the prep kernel.
   int* header;
+  int reuse_plan;  // 1: the workspace holds the prep kernel's plan from an earlier launch
   int grid_warps;  // warps of the main kernel's grid
   // [batch + 1] partitions of one head before sequence b; sequence b's partition k of head h
   // writes partial slot chunk_prefix[b] * H + h * parts_b + k, so a (sequence, head)'s partials
@@ -357,6 +360,10 @@ __global__ void __launch_bounds__(kPrepThreads) decode_prep_kernel(DecodeArgs a,
     a.header[0] = 0;
     a.header[1] = 0;
     a.header[4] = 0;
+    a.header[6] = a.batch;
+    a.header[7] = a.num_kv_heads;
+    a.header[8] = a.max_blocks;
+    a.header[9] = a.grid_warps;
   }
   __syncthreads();
   const int wsum = __reduce_add_sync(0xffffffffu, unsigned(sum));
@@ -441,6 +448,23 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int g = lane >> 2, t = lane & 3;
+  if (a.reuse_plan) {
+    // The plan must have been made for this batch, head count, table width and grid.
+    if (__ldg(a.header + 6) != a.batch || __ldg(a.header + 7) != a.num_kv_heads ||
+        __ldg(a.header + 8) != a.max_blocks || __ldg(a.header + 9) != a.grid_warps) {
+      if (blockIdx.x == 0 && threadIdx.x == 0) atomicExch(a.header + 1, 4);
+      return;
+    }
+    // Rows of empty contexts (no partition writes them): zeros, as the prep kernel writes them.
+    if (blockIdx.x == 0)
+      for (int b = threadIdx.x; b < a.batch; b += blockDim.x)
+        if (ctx_of(a, b) == 0)
+          for (int o = 0; o < (a.n_out > 0 ? a.n_out : 1); ++o)
+            for (int j = 0; j < a.num_q_heads; ++j) {
+              T* row = out_row<T, D>(a, o, b, j);
+              for (int e = 0; e < D; ++e) row[e] = ts::from_float<T>(0.f);
+            }
+  }
   uint8_t* ring = smem + warp * G::kRingBytes;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kWarps * G::kRingBytes) + warp * S;
   // Per stage: {partition, block | invalid flag, sequence, first block}, {first slot of its
@@ -862,20 +886,24 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
   } else if (cur_item >= 0) {
     finish_item();
   }
-  if (a.n_out > 0) {
-    // Every thread's output stores (local and peer) are made visible system-wide before its
-    // CTA counts itself done; the last CTA then publishes the epoch to every rank.
-    __threadfence_system();
-    __syncthreads();
-    if (threadIdx.x == 0) {
-      const int done = atomicAdd(a.header + 4, 1);
-      if (done == int(gridDim.x) - 1) {
+  // With peer outputs, every thread's output stores (local and peer) are made visible
+  // system-wide before its CTA counts itself done; the last CTA then publishes the epoch to
+  // every rank. The last CTA also re-zeroes the claim counter and this counter: every CTA has
+  // stopped claiming, and the next launch on the stream may reuse the plan.
+  if (a.n_out > 0) __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const int done = atomicAdd(a.header + 4, 1);
+    if (done == int(gridDim.x) - 1) {
+      if (a.n_out > 0) {
         __threadfence_system();
         for (int r = 0; r < a.n_out; ++r) {
           int* flag = a.signals[r] + a.signal_index;
           asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(flag), "r"(a.epoch) : "memory");
         }
       }
+      a.header[0] = 0;
+      a.header[4] = 0;
     }
   }
 }
@@ -942,8 +970,8 @@ bool make_pool_map(CUtensorMap* map, const void* pool, int64_t rows, int hd, int
 }
 
 template <typename T, int D, int NT>
-int launch_fast(const DecodeArgs& a, const CUtensorMap& km, const CUtensorMap& vm,
-                cudaStream_t s) {
+int launch_fast(DecodeArgs a, const CUtensorMap& km, const CUtensorMap& vm, cudaStream_t s,
+                bool plan = true) {
   using G = Geometry<D>;
   auto kern = paged_decode_kernel<T, D, NT>;
   // Once per device: later calls may be captured into a CUDA graph.
@@ -954,7 +982,8 @@ int launch_fast(const DecodeArgs& a, const CUtensorMap& km, const CUtensorMap& v
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, G::kSmemBytes);
     if (dev >= 0 && dev < 64) attr_done[dev] = true;
   }
-  decode_prep_kernel<T><<<1, kPrepThreads, 0, s>>>(a, a.num_q_heads * D);
+  a.reuse_plan = plan ? 0 : 1;
+  if (plan) decode_prep_kernel<T><<<1, kPrepThreads, 0, s>>>(a, a.num_q_heads * D);
   kern<<<num_sms(), kWarps * 32, G::kSmemBytes, s>>>(km, vm, a);
   return ts::launch_status("paged_decode");
 }
@@ -995,13 +1024,14 @@ extern "C" size_t ts_paged_decode_workspace_size(int32_t batch, int32_t num_q_he
   return ws_layout(batch, num_kv_heads, head_dim, max_blocks_per_seq, nt, num_sms() * kWarps).total;
 }
 
-extern "C" int ts_paged_decode(void* out, const void* query, int64_t query_token_stride,
-                               const void* key_pool, const void* value_pool,
-                               const int32_t* block_tables, int32_t max_blocks_per_seq,
-                               const int32_t* context_lens, int32_t batch, int32_t num_q_heads,
-                               int32_t num_kv_heads, int32_t head_dim, int32_t block_size,
-                               int64_t num_blocks, float scale, int32_t dtype, void* workspace,
-                               size_t workspace_bytes, void* stream) {
+namespace {
+
+int paged_decode_call(void* out, const void* query, int64_t query_token_stride,
+                      const void* key_pool, const void* value_pool, const int32_t* block_tables,
+                      int32_t max_blocks_per_seq, const int32_t* context_lens, int32_t batch,
+                      int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim,
+                      int32_t block_size, int64_t num_blocks, float scale, int32_t dtype,
+                      void* workspace, size_t workspace_bytes, void* stream, bool plan) {
   if (ts::dtype_size(dtype) == 0)
     return ts::set_error(TS_ERR_INVALID_ARGUMENT, "paged_decode: bad dtype %d", dtype);
   if (batch < 0 || num_q_heads <= 0 || num_kv_heads <= 0 || num_q_heads % num_kv_heads ||
@@ -1073,14 +1103,44 @@ extern "C" int ts_paged_decode(void* out, const void* query, int64_t query_token
   a.part_ml = reinterpret_cast<float2*>(ws + w.part_ml);
 #define TS_FAST(T)                                                             \
   if (head_dim == 128)                                                         \
-    return nt == 1 ? launch_fast<T, 128, 1>(a, km, vm, s)                      \
-                   : launch_fast<T, 128, 2>(a, km, vm, s);                     \
-  return nt == 1 ? launch_fast<T, 64, 1>(a, km, vm, s) : launch_fast<T, 64, 2>(a, km, vm, s);
+    return nt == 1 ? launch_fast<T, 128, 1>(a, km, vm, s, plan)                \
+                   : launch_fast<T, 128, 2>(a, km, vm, s, plan);               \
+  return nt == 1 ? launch_fast<T, 64, 1>(a, km, vm, s, plan)                   \
+                 : launch_fast<T, 64, 2>(a, km, vm, s, plan);
   if (dtype == TS_BFLOAT16) {
     TS_FAST(__nv_bfloat16)
   }
   TS_FAST(__half)
 #undef TS_FAST
+}
+
+}  // namespace
+
+extern "C" int ts_paged_decode(void* out, const void* query, int64_t query_token_stride,
+                               const void* key_pool, const void* value_pool,
+                               const int32_t* block_tables, int32_t max_blocks_per_seq,
+                               const int32_t* context_lens, int32_t batch, int32_t num_q_heads,
+                               int32_t num_kv_heads, int32_t head_dim, int32_t block_size,
+                               int64_t num_blocks, float scale, int32_t dtype, void* workspace,
+                               size_t workspace_bytes, void* stream) {
+  return paged_decode_call(out, query, query_token_stride, key_pool, value_pool, block_tables,
+                           max_blocks_per_seq, context_lens, batch, num_q_heads, num_kv_heads,
+                           head_dim, block_size, num_blocks, scale, dtype, workspace,
+                           workspace_bytes, stream, true);
+}
+
+extern "C" int ts_paged_decode_planned(void* out, const void* query, int64_t query_token_stride,
+                                       const void* key_pool, const void* value_pool,
+                                       const int32_t* block_tables, int32_t max_blocks_per_seq,
+                                       const int32_t* context_lens, int32_t batch,
+                                       int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim,
+                                       int32_t block_size, int64_t num_blocks, float scale,
+                                       int32_t dtype, void* workspace, size_t workspace_bytes,
+                                       void* stream) {
+  return paged_decode_call(out, query, query_token_stride, key_pool, value_pool, block_tables,
+                           max_blocks_per_seq, context_lens, batch, num_q_heads, num_kv_heads,
+                           head_dim, block_size, num_blocks, scale, dtype, workspace,
+                           workspace_bytes, stream, false);
 }
 
 // --------------------------------------------------------------------------- no-alloc variant
@@ -1253,7 +1313,7 @@ extern "C" int ts_paged_decode_peer(void* const* dst_outs, int32_t world, int32_
                                     int32_t batch, int32_t num_q_heads, int32_t num_kv_heads,
                                     int32_t head_dim, int32_t block_size, int64_t num_blocks,
                                     float scale, int32_t dtype, void* workspace,
-                                    size_t workspace_bytes, void* stream) {
+                                    size_t workspace_bytes, int32_t reuse_plan, void* stream) {
   if (world < 1 || world > 64 || rank < 0 || rank >= world || epoch == 0)
     return ts::set_error(TS_ERR_INVALID_ARGUMENT,
                          "paged_decode_peer: bad world %d / rank %d / epoch %u", world, rank, epoch);
@@ -1325,11 +1385,13 @@ extern "C" int ts_paged_decode_peer(void* const* dst_outs, int32_t world, int32_
   a.part_o = reinterpret_cast<float*>(ws + w.part_o);
   a.part_ml = reinterpret_cast<float2*>(ws + w.part_ml);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const bool plan = reuse_plan == 0;
 #define TS_FAST_PEER(T)                                                        \
   if (head_dim == 128)                                                         \
-    return nt == 1 ? launch_fast<T, 128, 1>(a, km, vm, s)                      \
-                   : launch_fast<T, 128, 2>(a, km, vm, s);                     \
-  return nt == 1 ? launch_fast<T, 64, 1>(a, km, vm, s) : launch_fast<T, 64, 2>(a, km, vm, s);
+    return nt == 1 ? launch_fast<T, 128, 1>(a, km, vm, s, plan)                \
+                   : launch_fast<T, 128, 2>(a, km, vm, s, plan);               \
+  return nt == 1 ? launch_fast<T, 64, 1>(a, km, vm, s, plan)                   \
+                 : launch_fast<T, 64, 2>(a, km, vm, s, plan);
   if (dtype == TS_BFLOAT16) {
     TS_FAST_PEER(__nv_bfloat16)
   }

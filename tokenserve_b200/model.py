@@ -199,14 +199,17 @@ class PagedLlamaRunner:
         return self.attend(layer, q, st)
 
     def attend(self, layer: int, q: torch.Tensor, st: DeviceStep) -> torch.Tensor:
-        """K2 on the decode rows and K3 on the prefill rows (the step's K/V already in the pool)."""
+        """K2 on the decode rows and K3 on the prefill rows (the step's K/V already in the pool).
+
+        Every layer of a step has the same block tables and context lengths, so layer 0's decode
+        call plans the work and the later layers reuse that plan from the workspace."""
         kp, vp = self.kv[layer, 0], self.kv[layer, 1]
         out = torch.empty(q.shape, dtype=q.dtype, device=q.device)
         nd = st.num_decode
         if nd:
             ws = self.workspace(nd, st.decode_tables.shape[1])
             ops.paged_decode(out[:nd], q[:nd], kp, vp, st.decode_tables, st.decode_ctx,
-                             self.scale, ws)  # fmt: skip
+                             self.scale, ws, reuse_plan=layer > 0)  # fmt: skip
         if st.num_prefill:
             ops.paged_prefill(out[nd:], q[nd:], kp, vp, st.prefill_tables, st.prefill_qsl,
                               st.prefill_ctx, st.max_query_len, self.scale)  # fmt: skip

@@ -39,6 +39,11 @@ _SIGNATURES: dict[str, tuple[object, list[object]]] = {
         [_p, _p, _i64, _p, _p, _p, _i32, _p, _i32, _i32, _i32, _i32, _i32, _i64, _f32, _i32,
          _p, _sz, _p],
     ),
+    "ts_paged_decode_planned": (
+        ctypes.c_int,
+        [_p, _p, _i64, _p, _p, _p, _i32, _p, _i32, _i32, _i32, _i32, _i32, _i64, _f32, _i32,
+         _p, _sz, _p],
+    ),
     "ts_paged_prefill": (
         ctypes.c_int,
         [_p, _p, _i64, _p, _p, _p, _i32, _p, _p, _i32, _i32, _i32, _i32, _i32, _i32, _i32,
@@ -52,7 +57,7 @@ _SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "ts_paged_decode_peer": (
         ctypes.c_int,
         [_p, _i32, _i32, _p, ctypes.c_uint32, _p, _i64, _p, _p, _p, _i32, _p, _i32, _i32, _i32,
-         _i32, _i32, _i64, _f32, _i32, _p, ctypes.c_size_t, _p],
+         _i32, _i32, _i64, _f32, _i32, _p, ctypes.c_size_t, _i32, _p],
     ),
     "ts_wait_peers": (ctypes.c_int, [_p, _i32, ctypes.c_uint32, _p, _p]),
     "ts_peer_alloc": (ctypes.c_int, [ctypes.c_size_t, ctypes.POINTER(ctypes.c_void_p)]),
@@ -188,8 +193,14 @@ def paged_decode(
     context_lens: torch.Tensor,
     scale: float,
     workspace: torch.Tensor | None,
+    reuse_plan: bool = False,
 ) -> None:
-    """K2: ``query [B, Hq, D]`` over each sequence's context -> ``out [B, Hq, D]``."""
+    """K2: ``query [B, Hq, D]`` over each sequence's context -> ``out [B, Hq, D]``.
+
+    ``reuse_plan=True`` runs the work plan an earlier call left in ``workspace`` (same block
+    tables, context lengths, batch, KV heads and table width: the later layers of one decode
+    step) and skips the prep kernel (``ts_paged_decode_planned``).
+    """
     nb, hkv, bs, d = _pool_dims(key_pool)
     hq = query.shape[1]
     qs = _rows(query, hq, d, "query")
@@ -200,7 +211,9 @@ def paged_decode(
     if context_lens.dtype != torch.int32:
         raise KernelError("context_lens must be int32")
     ws_bytes = 0 if workspace is None else workspace.numel() * workspace.element_size()
-    code = load_library().ts_paged_decode(
+    lib = load_library()
+    fn = lib.ts_paged_decode_planned if reuse_plan else lib.ts_paged_decode
+    code = fn(
         _ptr(out), _ptr(query), qs, _ptr(key_pool), _ptr(value_pool), _ptr(block_tables),
         block_tables.shape[1], _ptr(context_lens), query.shape[0], hq, hkv, d, bs, nb,
         float(scale), _dtype(key_pool), _ptr(workspace), ws_bytes, _stream(),

@@ -105,7 +105,7 @@ class PeerGather:
 
     def decode(self, p: int, query: torch.Tensor, key_pool: torch.Tensor, value_pool: torch.Tensor,
                block_tables: torch.Tensor, context_lens: torch.Tensor, scale: float,
-               workspace: torch.Tensor) -> int:  # fmt: skip
+               workspace: torch.Tensor, reuse_plan: bool = False) -> int:  # fmt: skip
         nb, hkv, bs, d = ops._pool_dims(key_pool)
         hq = query.shape[1]
         qs = ops._rows(query, hq, d, "query")
@@ -116,7 +116,7 @@ class PeerGather:
             ops._ptr(query), qs, ops._ptr(key_pool), ops._ptr(value_pool),
             ops._ptr(block_tables), block_tables.shape[1], ops._ptr(context_lens),
             query.shape[0], hq, hkv, d, bs, nb, float(scale), ops._dtype(key_pool),
-            ops._ptr(workspace), ws_bytes, ops._stream(),
+            ops._ptr(workspace), ws_bytes, int(reuse_plan), ops._stream(),
         )  # fmt: skip
         ops._check(code, "paged_decode_peer")
         return self.epoch
