@@ -59,9 +59,10 @@ def parse() -> argparse.Namespace:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--pool-blocks", type=int, default=65536)
     ap.add_argument("--skip-e2e", action="store_true", help="profiling runs only")
-    ap.add_argument("--collective", choices=["fused", "nccl"], default="fused",
+    ap.add_argument("--collective", choices=["auto", "fused", "nccl"], default="auto",
                     help="decode70b at N>1: decode writing every rank's output buffer over "
-                         "NVLink (fused) or decode + NCCL all-gather")  # fmt: skip
+                         "NVLink (fused) or decode + NCCL all-gather on a second stream; auto: "
+                         "fused below 8 ranks, NCCL at 8 (measured faster there)")  # fmt: skip
     ap.add_argument("--resident-layers", type=int, default=0,
                     help="decode70b: layer pools kept resident (0 = as many as fit); layers "
                          "cycle through them, each still read in full from HBM")  # fmt: skip
@@ -611,7 +612,8 @@ def run_decode70b(args: argparse.Namespace, world: int, rank: int, local: int) -
     made = [torch.cuda.Event() for _ in range(nbuf)]
     freed = [torch.cuda.Event() for _ in range(nbuf)]
     kv_bytes_rank = case.kv_bytes(2) * hkv_r // case.num_kv_heads
-    fused = world > 1 and args.collective == "fused"
+    collective = args.collective if args.collective != "auto" else ("nccl" if world >= 8 else "fused")
+    fused = world > 1 and collective == "fused"
     pg = None
     if fused:
         from tokenserve_b200.peer import PeerGather
@@ -680,7 +682,9 @@ def run_decode70b(args: argparse.Namespace, world: int, rank: int, local: int) -
     ag_t = (sum(a.elapsed_time(b) for st in ag_ev for a, b in st) / 1e3 / (args.steps * layers)
             if world > 1 else 0.0)  # fmt: skip
     stats = torch.tensor([elapsed, dec_t, ag_t], dtype=torch.float64, device=dev)
+    per_rank = [stats.clone() for _ in range(world)]
     if world > 1:
+        dist.all_gather(per_rank, stats)
         dist.all_reduce(stats, op=dist.ReduceOp.MAX)
     elapsed, dec_t, ag_t = stats.tolist()
     if rank == 0:
@@ -733,6 +737,9 @@ def run_decode70b(args: argparse.Namespace, world: int, rank: int, local: int) -
                           {"bytes_per_layer": ag_bytes, "avg_us": round(ag_t * 1e6, 2),
                            "algbw_gbs": round(ag_bytes / ag_t / 1e9, 1)}),
             # per layer K1 + decode (+ the peer wait), and one prep kernel per step (layer 0)
+            "per_rank_us": (None if world == 1 else
+                            [{"decode": round(float(x[1]) * 1e6, 1), "wait_or_gather": round(float(x[2]) * 1e6, 1)}
+                             for x in per_rank]),
             "gpu_launches": (((3 if fused else 2 + (2 if world > 1 else 0)) * layers) + 1) * args.steps,
             "clocks": clocks.summary(),
         }  # fmt: skip
