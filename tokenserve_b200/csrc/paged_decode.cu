@@ -10,16 +10,21 @@
 //   * Work item = partition of one (sequence b, KV head h): up to 64 consecutive blocks. All
 //     G = Hq/Hkv query heads of h are packed into the N dimension of the tensor-core tiles, so a
 //     KV byte serves every query head that uses it (GQA packing).
-//   * A one-CTA prep kernel splits the step's (sequence, head, block) units evenly over the
-//     grid's warps (static balance: every warp streams the same number of blocks whatever the
-//     batch) and cuts each warp's range into partitions at sequence-head ends and every 64
-//     blocks. Every warp is an independent pipeline over its own partitions: lane 0 streams
-//     their blocks with 2-D TMA loads (128-byte swizzle, no multicast) into a private ring of
-//     kStages stages, each holding one block's K and V tile for head h.
+//   * A one-CTA prep kernel plans the step into the workspace: small steps get a static even
+//     split of the (sequence, head, block) units over the grid's warps, cut into partitions at
+//     sequence ends and every 64 blocks; large steps get partitions of 64 / 32 / 16 blocks
+//     claimed from a counter in a sorted order. The plan depends only on the block tables and
+//     context lengths, so a model's later layers in the same step reuse it
+//     (ts_paged_decode_planned) and launch the decode kernel alone.
+//   * Every warp is an independent pipeline over its partitions: it fetches its next item a few
+//     blocks before the current one ends, and lane 0 streams the blocks with 2-D TMA loads
+//     (128-byte swizzle, no multicast) into a private ring of kStages stages, each holding one
+//     block's K and V tile for head h.
 //   * S^T = K Q^T and O^T += V^T P^T on mma.sync m16n8k16 (fp32 accumulate). P is split into a
 //     hi and a lo half-precision part so the PV product keeps ~16 mantissa bits.
 //   * Online softmax in fp32 (exp2 domain) per block; partitions of one (b, h) are merged by the
-//     last warp to finish one (log-sum-exp merge), tracked with an arrival counter.
+//     last warp to finish one (log-sum-exp merge in fixed partition order), tracked with an
+//     arrival counter.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -69,9 +74,8 @@ constexpr int kBlock = 16;                          // tokens per KV block
 //
 // Large steps instead use dynamic claiming (the split above would cut more sequences and leave
 // the partition merges unevenly spread): partitions of pb blocks (64 / 32 / 16, the largest that
-// gives every warp two), all full ones first and the partial last ones longest first, claimed
-// from a counter. The prep kernel picks the static split below kStaticMaxBlocksPerWarp blocks
-// per warp on average.
+// gives every warp two), claimed from a counter in the order prep_dynamic describes. The prep
+// kernel picks the static split below kStaticMaxBlocksPerWarp blocks per warp on average.
 constexpr int kPartBlocks = TS_DECODE_PART_BLOCKS;
 constexpr int kMinPartBlocks = 16;
 constexpr int kStaticMaxBlocksPerWarp = TS_DECODE_STATIC_MAX_BLOCKS;
