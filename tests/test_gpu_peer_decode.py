@@ -27,13 +27,13 @@ from tokenserve_b200.workloads import small_paged_case
 pytestmark = pytest.mark.gpu
 
 
-def _peer_call(lib, dst, world, rank, sig, epoch, q, kp, vp, bt, cl, scale, ws):  # type: ignore[no-untyped-def]
+def _peer_call(lib, dst, world, rank, sig, epoch, q, kp, vp, bt, cl, scale, ws, reuse=0):  # type: ignore[no-untyped-def]
     nb, hkv, bs, d = kp.shape
     code = lib.ts_paged_decode_peer(
         dst.data_ptr(), world, rank, sig.data_ptr(), epoch, q.data_ptr(), q.stride(0),
         kp.data_ptr(), vp.data_ptr(), bt.data_ptr(), bt.shape[1], cl.data_ptr(), q.shape[0],
         q.shape[1], hkv, d, bs, nb, scale, ops.TS_BFLOAT16, ws.data_ptr(),
-        ws.numel(), 0, torch.cuda.current_stream().cuda_stream,
+        ws.numel(), reuse, torch.cuda.current_stream().cuda_stream,
     )  # fmt: skip
     assert code == 0, lib.ts_last_error()
 
@@ -83,6 +83,57 @@ def test_peer_decode_writes_every_rank_buffer(cuda_device) -> None:  # type: ign
                                case.block_tables, case.context_lens, d**-0.5)  # fmt: skip
     err = np.abs(full[0].float().cpu().numpy() - ref)
     assert err.max() <= 2e-3 * np.abs(ref).max() + 2.0**-8 * np.abs(ref).max()
+
+
+def test_peer_decode_reuses_the_plan_across_layers(cuda_device) -> None:  # type: ignore[no-untyped-def]
+    """Two layers through the peer path, two ranks emulated on one GPU: layer 0 plans, layer 1
+    (other pools and queries, same tables) reuses each rank's plan. After each layer every
+    rank's full buffer equals the plain decodes of all ranks' heads, and the epoch advances."""
+    lib = ops.load_library()
+    hq, hkv, d, world = 16, 4, 128, 2
+    ctx = [5, 0, 333, 2100, 64, 700, 4100, 31]
+    case = small_paged_case(8, ctx, num_q_heads=hq, num_kv_heads=hkv, head_dim=d)
+    bt = torch.from_numpy(case.block_tables).to(cuda_device)
+    cl = torch.from_numpy(case.context_lens).to(cuda_device)
+    full = [torch.full((case.batch, hq, d), 7.0, dtype=torch.bfloat16, device=cuda_device)
+            for _ in range(world)]  # fmt: skip
+    sigs = [torch.zeros(world, dtype=torch.int32, device=cuda_device) for _ in range(world)]
+    dst = torch.tensor([f.data_ptr() for f in full], dtype=torch.int64, device=cuda_device)
+    sig = torch.tensor([s_.data_ptr() for s_ in sigs], dtype=torch.int64, device=cuda_device)
+    shards = [shard_heads(hq, hkv, world, r) for r in range(world)]
+    wss = [torch.empty(ops.decode_workspace_size(case.batch, sh.num_q_heads, sh.num_kv_heads, d,
+                                                 bt.shape[1], 16, torch.bfloat16),
+                       dtype=torch.uint8, device=cuda_device) for sh in shards]  # fmt: skip
+    status = torch.zeros(1, dtype=torch.int32, device=cuda_device)
+    for layer in range(2):
+        g = torch.Generator().manual_seed(40 + layer)
+        shape = (case.num_blocks, hkv, 16, d)
+        kp = (torch.randn(shape, generator=g) * 0.5).to(torch.bfloat16)
+        vp = (torch.randn(shape, generator=g) * 0.5).to(torch.bfloat16)
+        q = (torch.randn(case.batch, hq, d, generator=g) * 0.5).to(torch.bfloat16)
+        plain = []
+        for r, sh in enumerate(shards):
+            kr = shard_pool(kp, sh).to(cuda_device)
+            vr = shard_pool(vp, sh).to(cuda_device)
+            qr = q[:, sh.q_slice].contiguous().to(cuda_device)
+            _peer_call(lib, dst, world, r, sig, layer + 1, qr, kr, vr, bt, cl, d**-0.5, wss[r],
+                       reuse=int(layer > 0))  # fmt: skip
+            out = torch.empty_like(qr)
+            fresh = torch.empty_like(wss[r])
+            ops.paged_decode(out, qr, kr, vr, bt, cl, d**-0.5, fresh)
+            plain.append(out)
+        for r in range(world):
+            assert lib.ts_wait_peers(sigs[r].data_ptr(), world, layer + 1, status.data_ptr(),
+                                     torch.cuda.current_stream().cuda_stream) == 0  # fmt: skip
+        torch.cuda.synchronize()
+        assert int(status) == 0
+        assert all(s_.tolist() == [layer + 1] * world for s_ in sigs)
+        expect = torch.cat(plain, dim=1)
+        for f in full:
+            assert torch.equal(f, expect), f"layer {layer}"
+        for ws in wss:  # claim and CTA counters back at zero, no error
+            h = ws[:20].view(torch.int32).tolist()
+            assert h[0] == 0 and h[1] == 0 and h[4] == 0
 
 
 def test_wait_for_an_unpublished_epoch_times_out(cuda_device) -> None:  # type: ignore[no-untyped-def]
