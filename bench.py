@@ -43,7 +43,9 @@ WORKLOAD = "paged decode op, Llama-3-8B attention (32q/8kv, D=128, bf16, block 1
 def parse() -> argparse.Namespace:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=None,
+                    help="timed steps (default: 200 for the decode-op line, whose steps take "
+                         "~0.3 ms, so the clock sampler sees the timed region; 20 otherwise)")  # fmt: skip
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["cuda", "reference"], default="cuda")
     ap.add_argument("--workload",
@@ -69,7 +71,10 @@ def parse() -> argparse.Namespace:
     ap.add_argument("--shard-of", type=int, default=1,
                     help="decode70b on 1 GPU: run rank 0's share of an N-way KV-head split "
                          "(no collective), to measure the per-rank kernel alone")  # fmt: skip
-    return ap.parse_args()
+    args = ap.parse_args()
+    if args.steps is None:
+        args.steps = 200 if args.workload == "decode" and args.impl == "cuda" else 20
+    return args
 
 
 def peaks() -> tuple[float, str]:
