@@ -741,10 +741,10 @@ def run_decode70b(args: argparse.Namespace, world: int, rank: int, local: int) -
                           if fused else
                           {"bytes_per_layer": ag_bytes, "avg_us": round(ag_t * 1e6, 2),
                            "algbw_gbs": round(ag_bytes / ag_t / 1e9, 1)}),
-            # per layer K1 + decode (+ the peer wait), and one prep kernel per step (layer 0)
             "per_rank_us": (None if world == 1 else
                             [{"decode": round(float(x[1]) * 1e6, 1), "wait_or_gather": round(float(x[2]) * 1e6, 1)}
                              for x in per_rank]),
+            # per layer K1 + decode (+ the peer wait), and one prep kernel per step (layer 0)
             "gpu_launches": (((3 if fused else 2 + (2 if world > 1 else 0)) * layers) + 1) * args.steps,
             "clocks": clocks.summary(),
         }  # fmt: skip
