@@ -151,7 +151,9 @@ int ts_paged_decode_planned(void* out, const void* query, int64_t query_token_st
  *   - Sizes whose scratch (ts_paged_decode_workspace_size) exceeds TS_NO_ALLOC_SCRATCH_BYTES
  *     are rejected with TS_ERR_WORKSPACE_TOO_SMALL before anything is launched.
  *   - The first call on each device looks up the scratch's device address with that device
- *     current; make that first call before any stream capture.
+ *     current and keeps it for the life of the process; make that first call before any
+ *     stream capture. A cudaDeviceReset invalidates that address (and the kernel attributes
+ *     the library sets once per device): calls after a reset of the device are unsupported.
  *   - All calls on a device share the one scratch array and each call clears the parts that
  *     must start at zero. Calls whose kernels overlap on the GPU (different streams without
  *     ordering between them) race on it and give wrong results: order them.
@@ -255,8 +257,9 @@ int ts_verify_tags(const int32_t* tag_pool, const int32_t* block_tables,
  * rank's counts), except the output: each of dst_outs[0..world) is a rank's full output
  * [batch][world * num_q_heads][head_dim], and this rank's rows land at head offset
  * rank * num_q_heads in every one of them (stores over NVLink for the peers). The grid's last
- * CTA then writes `epoch` (non-zero, increasing per call) into signals[r][rank] for every r.
- * dst_outs and signals are device arrays of device pointers (peer buffers mapped with
+ * CTA then writes `epoch` (non-zero, increasing per call) into signals[r][rank] for every r;
+ * with batch 0 nothing is decoded and one small kernel publishes the epoch the same way, so the
+ * other ranks' waits still end. dst_outs and signals are device arrays of device pointers (peer buffers mapped with
  * ts_ipc_open); the tensor-core decode path is required (TS_ERR_UNSUPPORTED otherwise).
  * reuse_plan = 1 skips the prep kernel and runs the plan an earlier call left in `workspace`,
  * under the preconditions of ts_paged_decode_planned.

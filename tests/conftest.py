@@ -4,7 +4,8 @@
   else runs on the CPU.
 * Runs ``async def`` tests with ``asyncio.run`` (tokenserve's own suite uses pytest-asyncio,
   which is not available here).
-* Puts the repository root on ``sys.path`` so ``tokenserve_b200`` and ``oracle`` import.
+* Puts the repository root on ``sys.path`` so ``tokenserve_b200`` and ``oracle`` import, and
+  ``baseline/_ref`` (tokenserve itself) when it has been installed there.
 """
 
 from __future__ import annotations
@@ -19,6 +20,10 @@ import pytest
 ROOT = Path(__file__).resolve().parent.parent
 if str(ROOT) not in sys.path:
     sys.path.insert(0, str(ROOT))
+# tokenserve itself, installed unmodified by baseline/install_reference.py (when present).
+REF = ROOT / "baseline" / "_ref"
+if (REF / "tokenserve").is_dir() and str(REF) not in sys.path:
+    sys.path.append(str(REF))
 
 GOLDEN = ROOT / "tests" / "golden"
 

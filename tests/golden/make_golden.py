@@ -44,7 +44,9 @@ from pathlib import Path
 import numpy as np
 
 HERE = Path(__file__).resolve().parent
-sys.path.insert(0, os.environ.get("TOKENSERVE_SRC", "/root/reference/src"))
+if not os.environ.get("TOKENSERVE_SRC"):
+    sys.exit("make_golden.py: set TOKENSERVE_SRC to the reference tokenserve's src directory")
+sys.path.insert(0, os.environ["TOKENSERVE_SRC"])
 
 import torch  # noqa: E402
 import transformers  # noqa: E402

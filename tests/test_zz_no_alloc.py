@@ -4,8 +4,10 @@ The no-alloc entry point serves callers that cannot allocate a device workspace 
 for instance C code running inside a process whose device memory belongs to another
 framework's allocator, or a latency-critical loop that must not call cudaMalloc/cudaFree
 (they can synchronise the device). It runs the decode kernels with scratch held in a fixed
-array inside the library, so it must give the same attention output as the workspace entry
-point, call after call, and refuse sizes whose scratch does not fit that array.
+array inside the library. With the same inputs it runs the same kernels with the same plan and
+the same merge order as the workspace entry point, so its output must be bit-identical to it,
+call after call (a partial left in the shared array by an earlier call must not leak into a
+later one); it must also refuse sizes whose scratch does not fit that array.
 
 This file is collected last on purpose, so a run that stops at its first failure has run every
 other test already; it also passes on its own in a fresh process.
@@ -19,6 +21,7 @@ import numpy as np
 import pytest
 import torch
 
+from oracle.attention import paged_decode_np
 from tokenserve_b200 import ops
 from tokenserve_b200.workloads import small_paged_case
 
@@ -46,10 +49,14 @@ def call_no_alloc(fn, out, q, kp, vp, bt, cl, scale) -> int:  # type: ignore[no-
 
 
 @pytest.mark.parametrize(
-    ("dtype", "hq", "hkv"), [(torch.bfloat16, 32, 8), (torch.float16, 64, 8)]
+    ("dtype", "hq", "hkv", "d"),
+    [
+        (torch.bfloat16, 32, 8, 128),  # tensor-core kernel, scratch in the built-in array
+        (torch.float16, 64, 8, 128),  # tensor-core kernel, two query tiles per KV head
+        (torch.bfloat16, 8, 2, 256),  # head_dim 256: the CUDA-core kernel, which needs no scratch
+    ],
 )
-def test_no_alloc_decode_matches_workspace_decode_twice(cuda_device, dtype, hq, hkv) -> None:  # type: ignore[no-untyped-def]
-    d = 128
+def test_no_alloc_decode_matches_workspace_decode_twice(cuda_device, dtype, hq, hkv, d) -> None:  # type: ignore[no-untyped-def]
     ctx = [1, 16, 17, 255, 256, 700, 1500, 3000, 33, 4096, 90, 512]
     case = small_paged_case(31, ctx, num_q_heads=hq, num_kv_heads=hkv, head_dim=d)
     g = torch.Generator().manual_seed(4)
@@ -60,8 +67,9 @@ def test_no_alloc_decode_matches_workspace_decode_twice(cuda_device, dtype, hq, 
     cl = torch.from_numpy(case.context_lens).to(cuda_device)
     scale = d**-0.5
     need = ops.decode_workspace_size(case.batch, hq, hkv, d, bt.shape[1], 16, dtype)
-    assert 0 < need <= NO_ALLOC_SCRATCH_BYTES
-    ws = torch.empty(need, dtype=torch.uint8, device=cuda_device)
+    assert need <= NO_ALLOC_SCRATCH_BYTES
+    assert (need > 0) == (d == 128)
+    ws = torch.empty(need, dtype=torch.uint8, device=cuda_device) if need else None
     fn = bind()
     for call in range(2):  # two calls in a row share (and must reset) the built-in scratch
         q = (torch.randn(case.batch, hq, d, generator=g) * 0.5).to(dtype).to(cuda_device)
@@ -71,10 +79,17 @@ def test_no_alloc_decode_matches_workspace_decode_twice(cuda_device, dtype, hq, 
         rc = call_no_alloc(fn, out, q, kp, vp, bt, cl, scale)
         assert rc == 0, ops.load_library().ts_last_error().decode()
         torch.cuda.synchronize()
-        r = ref.float().cpu().numpy().astype(np.float64)
-        o = out.float().cpu().numpy().astype(np.float64)
-        tol = 2e-3 * np.abs(r).max() + HALF_ULP[dtype] * np.abs(r)
-        assert (np.abs(o - r) <= tol).all(), f"call {call}: max diff {np.abs(o - r).max():.3e}"
+        diff = (out.float() - ref.float()).abs().max().item()
+        assert torch.equal(out, ref), f"call {call}: differs from ts_paged_decode by {diff:.3e}"
+        if call == 1:
+            # The attention itself, against the float64 oracle (eager attention over the
+            # gathered context), with the tolerance of the kernel tests.
+            r = paged_decode_np(q.float().cpu().numpy(), kp.float().cpu().numpy(),
+                                vp.float().cpu().numpy(), case.block_tables, case.context_lens,
+                                scale)  # fmt: skip
+            o = out.float().cpu().numpy().astype(np.float64)
+            tol = 2e-3 * np.abs(r).max() + HALF_ULP[dtype] * np.abs(r)
+            assert (np.abs(o - r) <= tol).all(), f"max diff to oracle {np.abs(o - r).max():.3e}"
 
 
 def test_no_alloc_decode_rejects_sizes_beyond_its_scratch(cuda_device) -> None:  # type: ignore[no-untyped-def]

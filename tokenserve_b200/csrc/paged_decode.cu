@@ -912,6 +912,15 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
   }
 }
 
+// An empty batch still takes part in the exchange: the epoch is published to every rank, so
+// their waits for it end.
+__global__ void publish_epoch_kernel(int* const* signals, int world, int index, unsigned epoch) {
+  const int r = threadIdx.x;
+  if (r >= world) return;
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(signals[r] + index), "r"(epoch)
+               : "memory");
+}
+
 // Waits until every rank has published `epoch` into signals[0..world) (this rank's signal
 // array, written by the ranks' decode kernels), with a bounded spin: on timeout *status = 3.
 __global__ void wait_peers_kernel(const int* signals, int world, unsigned epoch, int* status) {
@@ -1343,7 +1352,11 @@ extern "C" int ts_paged_decode_peer(void* const* dst_outs, int32_t world, int32_
   if (batch > 8192 || int64_t(batch) * max_blocks_per_seq >= (int64_t(1) << 31) ||
       max_blocks_per_seq > (1 << 20) || num_sms() * kWarps > kMaxGridWarps)
     return ts::set_error(TS_ERR_UNSUPPORTED, "paged_decode_peer: sizes too large");
-  if (batch == 0) return ts::ok();
+  if (batch == 0) {
+    publish_epoch_kernel<<<1, 64, 0, static_cast<cudaStream_t>(stream)>>>(
+        reinterpret_cast<int* const*>(signals), world, rank, epoch);
+    return ts::launch_status("paged_decode_peer");
+  }
   const int group = num_q_heads / num_kv_heads;
   const int nt = group > 8 ? 2 : 1;
   const WsLayout w =

@@ -382,6 +382,9 @@ class DecodeGraphs:
         nb = plan.num_decode
         b = _bucket(nb, 8)
         w = min(_pow2_bucket(plan.width), self.mirror.max_cols)
+        # The mirror already counts this step's new table entries as uploaded (plan_decode),
+        # so they are applied before anything that can fail, such as capturing a new graph.
+        self._apply_deltas(plan.deltas)
         g = self.graphs.get((b, w))
         if g is None:
             g = self.graphs[(b, w)] = self._capture(b, w)
@@ -400,7 +403,6 @@ class DecodeGraphs:
         rows[nb:] = 0
         dctx[:nb] = torch.from_numpy(plan.decode_ctx)
         dctx[nb:] = 0
-        self._apply_deltas(plan.deltas)
         g["meta"].copy_(hv, non_blocking=True)
         g["graph"].replay()
         return g["logits"][:nb], g["tokens"][:nb]

@@ -127,8 +127,11 @@ class PeerGather:
         ops._check(code, "wait_peers")
 
     def check(self) -> None:
-        """Raises if any wait timed out (a rank that never published its epoch)."""
-        if int(self.status.item()):
+        """Raises if any wait since the last check timed out (a rank that never published its
+        epoch); the status word is cleared either way, so one timeout is reported once."""
+        code = int(self.status.item())
+        if code:
+            self.status.zero_()
             raise ops.KernelError("wait_peers: a rank did not publish its output in time")
 
     def close(self) -> None:
