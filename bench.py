@@ -13,8 +13,17 @@ with inputs resident in HBM. ``e2e`` = the same bytes / step time through the C-
 pinned host buffers, H2D of the step's inputs and D2H of the attention output inside the timed
 region. ``roofline`` covers the decode kernel alone.
 
-Multi-GPU (torchrun): every rank runs its own seeded batch of 256 sequences (sequences are
-independent, so the path shards without any data-path collective; scaling is weak).
+Multi-GPU (torchrun): the same batch of 256 sequences with its KV heads sharded over the ranks
+(strong scaling): rank r of N holds KV heads [r*8/N, (r+1)*8/N) and their query heads under
+the same block tables, runs K1 + K2 on them, and the step's [B, 32/N, D] outputs are
+all-gathered so every rank ends the step with the full [B, 32, D] — fused into the decode as
+stores over NVLink into every rank's buffer (``--collective fused``) or an NCCL all-gather on a
+second stream (``nccl``). After timing, the gathered output is compared bit for bit with the
+ranks' own decodes brought together by an independent all-gather.
+
+After the timed region, the oracle (float64 eager attention over the gathered context) checks
+the last timed launch's output for the 24 longest sequences and 24 others, and the appended
+K/V rows are checked bit for bit (``parity`` in the line).
 
 ``--impl reference`` times the CPU oracle (a restatement of transformers' eager attention over
 the gathered context, which is what tokenserve's HFBackend runs) on a bounded sample of the
@@ -50,21 +59,26 @@ def parse() -> argparse.Namespace:
     ap.add_argument("--impl", choices=["cuda", "reference"], default="cuda")
     ap.add_argument("--workload",
                     choices=["decode", "prefill", "decode70b", "engine-tiny", "engine-8b",
-                             "kv-ops", "swap"],
+                             "engine-tiny-replay", "engine-8b-replay", "kv-ops", "swap"],
                     default="decode",
                     help="decode: the headline decode-op line; prefill: chunked prefill with a "
                          "1024-token cached prefix, 32 layers")  # fmt: skip
     ap.add_argument("--layers", type=int, default=32, help="prefill workload only")
+    ap.add_argument("--no-extras", action="store_true",
+                    help="decode line at N=1: leave out the prefill, engine_tiny and engine_8b "
+                         "sub-objects")  # fmt: skip
     ap.add_argument("--replays", type=int, default=1, help="engine workloads only")
     ap.add_argument("--batch", type=int, default=256)
     ap.add_argument("--cpu-sample-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--pool-blocks", type=int, default=65536)
     ap.add_argument("--skip-e2e", action="store_true", help="profiling runs only")
+    ap.add_argument("--skip-parity", action="store_true",
+                    help="profiling runs only: no oracle check of the timed output")  # fmt: skip
     ap.add_argument("--collective", choices=["auto", "fused", "nccl"], default="auto",
-                    help="decode70b at N>1: decode writing every rank's output buffer over "
-                         "NVLink (fused) or decode + NCCL all-gather on a second stream; auto: "
-                         "fused below 8 ranks, NCCL at 8 (measured faster there)")  # fmt: skip
+                    help="decode and decode70b at N>1: decode writing every rank's output "
+                         "buffer over NVLink (fused) or decode + NCCL all-gather on a second "
+                         "stream; auto: fused below 8 ranks, NCCL at 8")  # fmt: skip
     ap.add_argument("--resident-layers", type=int, default=0,
                     help="decode70b: layer pools kept resident (0 = as many as fit); layers "
                          "cycle through them, each still read in full from HBM")  # fmt: skip
@@ -119,12 +133,22 @@ def measured_traffic(decode_bytes: int) -> int | None:
 def config(args: argparse.Namespace, n: int) -> dict:
     return {
         "workload": WORKLOAD,
-        "batch_per_gpu": args.batch,
-        "global_batch": args.batch * n,
+        "global_batch": args.batch,
         "context": "log-normal median 1024 sigma 1.0 clipped 16..8192",
         "l2": "inputs larger than L2 (~1.7 GB KV read per step), no flush",
-        "parallelism": f"independent sequence batches x{n}" if n > 1 else "single GPU",
-    }
+        "parallelism": ("single GPU" if n == 1 else
+                        f"KV-head sharding x{n}: each rank holds {8 // n} of the 8 KV heads and "
+                        f"their {32 // n} query heads for all {args.batch} sequences, under the "
+                        "same block tables; the step's [B, Hq/N, D] outputs are all-gathered"),
+    }  # fmt: skip
+
+
+def collective_for(args: argparse.Namespace, world: int) -> str:
+    if world == 1:
+        return "none"
+    if args.collective != "auto":
+        return args.collective
+    return "nccl" if world >= 8 else "fused"
 
 
 # ----------------------------------------------------------------------------- CPU side
@@ -284,9 +308,13 @@ def main() -> None:
     if args.workload == "decode70b":
         run_decode70b(args, world, rank, local)
         return
-    if args.workload.startswith("engine"):
+    if args.workload.endswith("-replay"):
         if rank == 0:
             run_engine(args, local)
+        return
+    if args.workload.startswith("engine"):
+        if rank == 0:
+            run_engine_live(args, local)
         return
     if args.workload == "kv-ops":
         if rank == 0:
@@ -300,7 +328,52 @@ def main() -> None:
         if rank == 0:
             run_reference(args, world)
         return
-    run_cuda(args, world, rank, local)
+    line = run_cuda(args, world, rank, local)
+    if line is None:
+        return
+    if world == 1 and not args.no_extras:
+        add_extras(args, line, local)
+    print(json.dumps(line), flush=True)
+
+
+def add_extras(args: argparse.Namespace, line: dict, local: int) -> None:
+    """The other measured configurations as sub-objects of the default line (N=1): chunked
+    prefill (TFLOP/s, roofline, parity), the tiny-Llama engine (tokens/s, greedy parity, the
+    reference's own HFBackend on the host cores) and the Llama-3-8B engine (open loop at 20
+    req/s: tokens/s, TTFT, TPOT). A failing part is reported as an error, not dropped."""
+    import traceback
+
+    import torch
+
+    dev = torch.device("cuda", local)
+    parts = {
+        "prefill": lambda: prefill_extra(args, dev),
+        "engine_tiny": lambda: engine_tiny_live(dev, not args.no_cpu_baseline,
+                                                args.cpu_sample_seconds),
+        "engine_8b": lambda: engine_8b_live(dev),
+    }  # fmt: skip
+    for name, fn in parts.items():
+        try:
+            line[name] = fn()
+        except Exception as e:  # noqa: BLE001 - reported in the line
+            line[name] = {"error": f"{type(e).__name__}: {e}",
+                          "trace": traceback.format_exc(limit=3)[-600:]}  # fmt: skip
+        torch.cuda.empty_cache()
+
+
+def prefill_extra(args: argparse.Namespace, dev) -> dict:  # type: ignore[no-untyped-def]
+    steps = 5
+    res = prefill_measure(args, dev, steps, 3, parity=True)
+    return {
+        "metric": PREFILL_METRIC,
+        "workload": "chunked prefill with prefix cache, Llama-3-8B attention (32q/8kv, D=128, "
+                    "bf16, block 16): 64 sequences, 1024-token cached prefix, suffixes "
+                    "256..2048 in 512-token chunks, 32 layers",
+        "value": round(res["flops_step"] * steps / res["elapsed"] / 1e12, 2), "unit": "TFLOP/s",
+        "steps": steps, "ms_per_step": round(1000 * res["elapsed"] / steps, 3),
+        "roofline": prefill_roofline(res, steps), "parity": res.get("parity"),
+        "gpu_launches": 2 * res["launches"], "clocks": res["clocks"].summary(),
+    }  # fmt: skip
 
 
 def run_reference(args: argparse.Namespace, world: int) -> None:
@@ -344,7 +417,7 @@ def run_reference(args: argparse.Namespace, world: int) -> None:
         "warmup": args.warmup,
         "ms_per_step": round(1000 * total / args.steps, 3),
         "higher_is_better": True,
-        "scaling": "weak",
+        "scaling": "weak" if world == 1 else "strong",
         "vs_baseline": None,
         "dtype": "f32 (bf16 inputs upcast, as HFBackend's float32 eager attention)",
         "data": "synthetic",
@@ -356,24 +429,91 @@ def run_reference(args: argparse.Namespace, world: int) -> None:
     }))  # fmt: skip
 
 
-def run_cuda(args: argparse.Namespace, world: int, rank: int, local: int) -> None:
+# ----------------------------------------------------------------------------- parity
+
+
+def parity_sample(context_lens: np.ndarray, n: int = 48) -> list[int]:
+    """The n // 2 longest sequences plus n // 2 spread evenly over the rest (batch order)."""
+    order = np.argsort(-context_lens.astype(np.int64), kind="stable")
+    longest = [int(b) for b in order[: n // 2]]
+    rest = [b for b in range(len(context_lens)) if b not in set(longest)]
+    if rest:
+        idx = np.linspace(0, len(rest) - 1, min(n - len(longest), len(rest))).round().astype(int)
+        longest += [rest[i] for i in sorted(set(idx.tolist()))]
+    return sorted(longest)
+
+
+def decode_parity(case, out, q, kpool, vpool, scale, seqs):  # type: ignore[no-untyped-def]
+    """The oracle checks a timed launch's output, after the timed region.
+
+    ``out``/``q`` are ``[B, Hq_r, D]`` for the KV heads of ``kpool``/``vpool`` (one rank's share
+    of the heads, or all of them). Each checked sequence's blocks are copied to the host and
+    the oracle (float64 eager attention over the gathered context, transformers'
+    ``eager_attention_forward`` restated) recomputes its output rows. Tolerance, per element:
+    ``|out - ref| <= 2e-3 * max|ref| + 2^-8 * |ref|`` (2e-3 arithmetic, half a bf16 ulp for the
+    stored output).
+    """
+    import torch
+
+    from oracle.attention import paged_decode_np
+
+    bs = case.block_size
+    errs, refs = [], []
+    for b in seqs:
+        ctx = int(case.context_lens[b])
+        nblk = (ctx + bs - 1) // bs
+        ids = torch.from_numpy(case.block_tables[b, :nblk].astype(np.int64)).to(kpool.device)
+        ks = kpool.index_select(0, ids).float().cpu().numpy()
+        vs = vpool.index_select(0, ids).float().cpu().numpy()
+        r = paged_decode_np(q[b : b + 1].float().cpu().numpy(), ks, vs,
+                            [np.arange(nblk, dtype=np.int64)], [ctx], scale)[0]  # fmt: skip
+        o = out[b].float().cpu().numpy().astype(np.float64)
+        errs.append(np.abs(o - r))
+        refs.append(np.abs(r))
+    err, ref = np.stack(errs), np.stack(refs)
+    max_ref = float(ref.max())
+    tol = 2e-3 * max_ref + 2.0**-8 * ref
+    big = ref >= 0.1 * max_ref
+    return {
+        "ok": bool((err <= tol).all()),
+        "seqs_checked": len(seqs),
+        "contexts_checked": [int(case.context_lens[seqs].min()), int(case.context_lens[seqs].max())],
+        "max_abs_err_over_max_ref": float(err.max() / max_ref),
+        "max_rel_err": float((err[big] / ref[big]).max()),
+        "max_err_over_tolerance": float((err / tol).max()),
+        "tolerance": "|out - ref| <= 2e-3 * max|ref| + 2^-8 * |ref| (float64 oracle)",
+    }  # fmt: skip
+
+
+def k1_bitexact(kpool, vpool, knew, vnew, slots, bs: int) -> bool:  # type: ignore[no-untyped-def]
+    """Whether the K/V rows K1 appended (one per sequence) sit bit-exactly at their slots."""
+    import torch
+
+    blk, off = slots // bs, slots % bs
+    return bool(torch.equal(kpool[blk, :, off, :], knew) and torch.equal(vpool[blk, :, off, :], vnew))
+
+
+def run_cuda(args: argparse.Namespace, world: int, rank: int, local: int) -> dict | None:
+    import datetime
+
     import torch
     import torch.distributed as dist
 
     from tokenserve_b200 import ops
+    from tokenserve_b200.sharding import gather_heads, heads_from_gathered, shard_heads
     from tokenserve_b200.workloads import decode_workload
 
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     if world > 1:
-        import datetime
-
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
-                                device_id=dev)  # fmt: skip
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
     ops.load_library()
 
-    case = decode_workload(seed=rank, batch=args.batch, num_blocks=args.pool_blocks)
-    B, hq, hkv, d, bs = case.batch, case.num_q_heads, case.num_kv_heads, case.head_dim, 16
+    # Every rank runs the same seeded batch (the block tables and slots are replicated, as the
+    # scheduler's decisions are); rank r holds KV heads [r*8/N, (r+1)*8/N) and their query heads.
+    case = decode_workload(seed=0, batch=args.batch, num_blocks=args.pool_blocks)
+    sh = shard_heads(case.num_q_heads, case.num_kv_heads, world, rank)
+    B, hq, hkv, d, bs = case.batch, sh.num_q_heads, sh.num_kv_heads, case.head_dim, 16
     dt = torch.bfloat16
     g = torch.Generator(device=dev).manual_seed(1000 + rank)
     shape = (case.num_blocks, hkv, bs, d)
@@ -388,19 +528,66 @@ def run_cuda(args: argparse.Namespace, world: int, rank: int, local: int) -> Non
     slots = torch.from_numpy(case.append_slots).to(dev)
     bt = torch.from_numpy(case.block_tables).to(dev)
     cl = torch.from_numpy(case.context_lens).to(dev)
-    out = torch.empty(B, hq, d, dtype=dt, device=dev)
     ws = torch.empty(ops.decode_workspace_size(B, hq, hkv, d, bt.shape[1], bs, dt),
                      dtype=torch.uint8, device=dev)  # fmt: skip
     scale = d**-0.5
-    kv_bytes = case.kv_bytes(2)
-    # Algorithmic bytes of one decode launch: KV read + q in + out + block-table entries.
+    kv_bytes = case.kv_bytes(2)  # all 8 KV heads: what the whole job reads per step
+    kv_bytes_rank = kv_bytes * hkv // case.num_kv_heads
+    # Algorithmic bytes of one decode launch on this rank: its KV read + q in + out rows +
+    # block-table entries and context lengths.
     blocks_read = int(((case.context_lens.astype(np.int64) + bs - 1) // bs).sum())
-    decode_bytes = kv_bytes + 2 * B * hq * d * 2 + blocks_read * 4 + B * 4
+    decode_bytes = kv_bytes_rank + 2 * B * hq * d * 2 + blocks_read * 4 + B * 4
     stream = torch.cuda.current_stream()
+    collective = collective_for(args, world)
 
-    def step() -> None:
-        ops.reshape_and_cache(knew, vnew, kpool, vpool, slots)
-        ops.paged_decode(out, q, kpool, vpool, bt, cl, scale, ws)
+    # The step's output: out [B, Hq, D] at N=1; at N>1 each rank ends the step holding the full
+    # [B, 32, D] of every rank's heads (nbuf rotating buffers, so the gather of step i may
+    # overlap step i+1).
+    nbuf = 2
+    pg = None
+    if collective == "fused":
+        from tokenserve_b200.peer import PeerGather
+
+        pg = PeerGather(B, hq, d, dt, nbuf=nbuf)
+        full = pg.full
+    else:
+        full = [torch.empty(B, hq * world, d, dtype=dt, device=dev) for _ in range(nbuf)]
+    outs = [torch.empty(B, hq, d, dtype=dt, device=dev) for _ in range(nbuf)]
+    gath = [torch.empty(world, B, hq, d, dtype=dt, device=dev) for _ in range(nbuf)]
+    comm = torch.cuda.Stream(device=dev)
+    made = [torch.cuda.Event() for _ in range(nbuf)]
+    freed = [torch.cuda.Event() for _ in range(nbuf)]
+
+    def decode(i: int, qq, out_ev=None, ex_ev=None):  # type: ignore[no-untyped-def]
+        """K2 for step i (+ the exchange at N>1); returns the buffer holding the output."""
+        p = i % nbuf
+        if world == 1:
+            ops.paged_decode(outs[p], qq, kpool, vpool, bt, cl, scale, ws)
+            if out_ev is not None:
+                out_ev.record(stream)
+            return outs[p]
+        if pg is not None:
+            epoch = pg.decode(p, qq, kpool, vpool, bt, cl, scale, ws)
+            if out_ev is not None:
+                out_ev.record(stream)
+            pg.wait(epoch)
+            if ex_ev is not None:
+                ex_ev.record(stream)
+            return full[p]
+        if i >= nbuf:
+            stream.wait_event(freed[p])  # the gather of step i - nbuf has read outs[p]
+        ops.paged_decode(outs[p], qq, kpool, vpool, bt, cl, scale, ws)
+        if out_ev is not None:
+            out_ev.record(stream)
+        made[p].record(stream)
+        with torch.cuda.stream(comm):
+            comm.wait_event(made[p])
+            gather_heads(outs[p], gath[p])
+            full[p].copy_(heads_from_gathered(gath[p]))
+            freed[p].record(comm)
+            if ex_ev is not None:
+                ex_ev.record(comm)
+        return full[p]
 
     def barrier() -> None:
         if world > 1:
@@ -408,35 +595,75 @@ def run_cuda(args: argparse.Namespace, world: int, rank: int, local: int) -> Non
         torch.cuda.synchronize()
 
     # ---- device-resident timing
-    for _ in range(max(args.warmup, 3)):
-        step()
+    for i in range(max(args.warmup, 3)):
+        ops.reshape_and_cache(knew, vnew, kpool, vpool, slots)
+        decode(i, q)
+    stream.wait_stream(comm)
     barrier()
-    ev = [torch.cuda.Event(enable_timing=True) for _ in range(2 * args.steps + 2)]
+    n_ev = args.steps
+    t_k1 = [torch.cuda.Event(enable_timing=True) for _ in range(n_ev)]
+    t_dec = [torch.cuda.Event(enable_timing=True) for _ in range(n_ev)]
+    t_ex = [torch.cuda.Event(enable_timing=True) for _ in range(n_ev)]
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(dev) as clocks:
-        ev[0].record(stream)
+        e0.record(stream)
         for i in range(args.steps):
             ops.reshape_and_cache(knew, vnew, kpool, vpool, slots)
-            ev[2 + 2 * i].record(stream)
-            ops.paged_decode(out, q, kpool, vpool, bt, cl, scale, ws)
-            ev[3 + 2 * i].record(stream)
-        ev[1].record(stream)
+            t_k1[i].record(stream)
+            last = decode(i, q, t_dec[i], t_ex[i] if world > 1 else None)
+        stream.wait_stream(comm)
+        e1.record(stream)
         torch.cuda.synchronize()
     barrier()
-    elapsed = ev[0].elapsed_time(ev[1]) / 1e3
-    dec_ms = [ev[2 + 2 * i].elapsed_time(ev[3 + 2 * i]) for i in range(args.steps)]
-    dec_avg = sum(dec_ms) / len(dec_ms) / 1e3
+    elapsed = e0.elapsed_time(e1) / 1e3
+    # decode launch = from the end of K1 to the end of K2 (prep kernel included, as in a step)
+    dec_avg = sum(t_k1[i].elapsed_time(t_dec[i]) for i in range(n_ev)) / n_ev / 1e3
+    ex_avg = (sum(t_dec[i].elapsed_time(t_ex[i]) for i in range(n_ev)) / n_ev / 1e3
+              if world > 1 else None)  # fmt: skip
+
+    # ---- checks of the timed launches' output (outside the timed region)
+    checks: dict = {}
+    if pg is not None:
+        try:
+            pg.check()
+            checks["peer_waits_ok"] = True
+        except ops.KernelError:
+            checks["peer_waits_ok"] = False
+    k1_ok = k1_bitexact(kpool, vpool, knew, vnew, slots, bs)
+    if world > 1:
+        # The gathered [B, 32, D] must equal, bit for bit, every rank's own decode of its heads
+        # brought together by an independent NCCL all-gather.
+        ref_loc = torch.empty(B, hq, d, dtype=dt, device=dev)
+        ops.paged_decode(ref_loc, q, kpool, vpool, bt, cl, scale, ws)
+        ref_full = heads_from_gathered(gather_heads(ref_loc))
+        flags = torch.tensor([int(torch.equal(last, ref_full)), int(k1_ok),
+                              int(checks.get("peer_waits_ok", True))], device=dev)  # fmt: skip
+        dist.all_reduce(flags, op=dist.ReduceOp.MIN)
+        gather_ok, k1_ok, waits_ok = (bool(x) for x in flags.tolist())
+        checks.update(gather_bitexact=gather_ok, peer_waits_ok=waits_ok)
+    checks["k1_bitexact"] = k1_ok
+    if rank == 0 and not args.skip_parity:
+        mine = last[:, sh.q_slice] if world > 1 else last
+        checks.update(decode_parity(case, mine, q, kpool, vpool, scale,
+                                    parity_sample(case.context_lens)))  # fmt: skip
+        checks["heads_checked"] = f"query heads {sh.q_start}..{sh.q_start + hq - 1} (rank 0)"
+    # No rank may start the next decodes (which store into every rank's buffers) while rank 0
+    # still reads its buffer for the check.
+    barrier()
 
     if args.skip_e2e:
-        if rank == 0:
-            print(json.dumps({"profiling_run": True, "decode_avg_us": dec_avg * 1e6,
-                              "decode_bytes": decode_bytes}))  # fmt: skip
-        return
+        if pg is not None:
+            pg.close()
+        if world > 1:
+            dist.destroy_process_group()
+        return ({"profiling_run": True, "decode_avg_us": dec_avg * 1e6,
+                 "decode_bytes": decode_bytes, "parity": checks} if rank == 0 else None)  # fmt: skip
     # ---- end to end through the C-ABI with host buffers
-    # Every step copies its inputs from pinned host memory and its attention output back to
-    # the host. As a serving loop would, the copies run on their own streams with two buffer
-    # sets, so step i+1's upload and step i-1's download overlap step i's kernels.
-    # A step's six inputs sit in one pinned host buffer (256-byte aligned sections) and go up
-    # with ONE copy into the matching device buffer; the kernels read views of it.
+    # Every step copies its inputs from pinned host memory and its attention output (the full
+    # [B, 32, D] at N>1) back to the host. As a serving loop would, the copies run on their own
+    # streams with two buffer sets, so step i+1's upload and step i-1's download overlap step
+    # i's kernels. A step's six inputs sit in one pinned host buffer (256-byte aligned
+    # sections) and go up with ONE copy into the matching device buffer.
     srcs = (q, knew, vnew, slots, bt, cl)
     offs, o = [], 0
     for t in srcs:
@@ -452,14 +679,16 @@ def run_cuda(args: argparse.Namespace, world: int, rank: int, local: int) -> Non
         dst.copy_(src.cpu())
     d_buf = [torch.empty(o, dtype=torch.uint8, device=dev) for _ in range(2)]
     d_in = [views(b) for b in d_buf]
-    h_out = [torch.empty(out.shape, dtype=dt).pin_memory() for _ in range(2)]
-    d_out = [torch.empty_like(out) for _ in range(2)]
+    out_shape = (B, hq * world, d)
+    h_out = [torch.empty(out_shape, dtype=dt).pin_memory() for _ in range(2)]
+    d_out = [torch.empty(out_shape, dtype=dt, device=dev) for _ in range(2)]
     h2d = o  # the packed buffer: the six inputs plus alignment padding
     d2h = h_out[0].numel() * h_out[0].element_size()
     up, down = torch.cuda.Stream(device=dev), torch.cuda.Stream(device=dev)
     uploaded = [torch.cuda.Event() for _ in range(2)]
     computed = [torch.cuda.Event() for _ in range(2)]
     fetched = [torch.cuda.Event() for _ in range(2)]
+    step_no = [0]
 
     def e2e_run(n: int) -> None:
         for i in range(n):
@@ -474,7 +703,15 @@ def run_cuda(args: argparse.Namespace, world: int, rank: int, local: int) -> Non
                 stream.wait_event(fetched[p])  # step i-2's output has left d_out[p]
             dq, dk, dv, ds, dbt, dcl = d_in[p]
             ops.reshape_and_cache(dk, dv, kpool, vpool, ds)
-            ops.paged_decode(d_out[p], dq, kpool, vpool, dbt, dcl, scale, ws)
+            if world == 1:
+                ops.paged_decode(d_out[p], dq, kpool, vpool, dbt, dcl, scale, ws)
+            else:
+                res = decode(step_no[0], dq)
+                step_no[0] += 1
+                stream.wait_stream(comm)
+                # copied out on the compute stream before this rank's next decode, so no
+                # rank's next stores into the gather buffer can overtake the download
+                d_out[p].copy_(res)
             computed[p].record(stream)
             with torch.cuda.stream(down):
                 down.wait_event(computed[p])
@@ -488,19 +725,35 @@ def run_cuda(args: argparse.Namespace, world: int, rank: int, local: int) -> Non
     barrier()
     t_e2e = time.perf_counter()
     e2e_run(args.steps)
-    e2e_wall = time.perf_counter() - t_e2e
+    e2e_elapsed = time.perf_counter() - t_e2e
     barrier()
-    e2e_elapsed = e2e_wall
+    if pg is not None:
+        try:
+            pg.check()
+        except ops.KernelError:
+            checks["peer_waits_ok"] = False
 
+    per_rank = None
     if world > 1:
         t = torch.tensor([elapsed, e2e_elapsed], dtype=torch.float64, device=dev)
+        mine_t = torch.tensor([dec_avg, ex_avg if ex_avg is not None else -1.0],
+                              dtype=torch.float64, device=dev)  # fmt: skip
+        allr = [torch.empty_like(mine_t) for _ in range(world)]
+        dist.all_gather(allr, mine_t)
+        per_rank = [{"decode_us": round(float(x[0]) * 1e6, 2),
+                     "exchange_wait_us": round(float(x[1]) * 1e6, 2) if x[1] >= 0 else None}
+                    for x in allr]  # fmt: skip
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         elapsed, e2e_elapsed = t.tolist()
+        ok = torch.tensor([int(checks.get("peer_waits_ok", True))], device=dev)
+        dist.all_reduce(ok, op=dist.ReduceOp.MIN)
+        checks["peer_waits_ok"] = bool(ok.item())
 
     if rank == 0:
         peak, peak_kind = peaks()
         achieved = decode_bytes / dec_avg / 1e9
-        value = world * kv_bytes * args.steps / elapsed / 1e9
+        value = kv_bytes * args.steps / elapsed / 1e9
+        launches = 3 if world == 1 else (4 if pg is not None else 3)
         line = {
             "metric": METRIC,
             "value": round(value, 2),
@@ -510,7 +763,7 @@ def run_cuda(args: argparse.Namespace, world: int, rank: int, local: int) -> Non
             "warmup": max(args.warmup, 3),
             "ms_per_step": round(1000 * elapsed / args.steps, 4),
             "higher_is_better": True,
-            "scaling": "weak",
+            "scaling": "weak" if world == 1 else "strong",
             "vs_baseline": None,
             "dtype": "bf16",
             "data": "synthetic",
@@ -527,9 +780,12 @@ def run_cuda(args: argparse.Namespace, world: int, rank: int, local: int) -> Non
                 "traffic": None,
                 "algorithmic_bytes_per_launch": decode_bytes,
                 "avg_launch_us": round(dec_avg * 1e6, 2),
+                "launch": "prep + decode kernels, CUDA events on the launching stream"
+                          + ("" if world == 1 else "; rank 0's heads"),
             },
+            "parity": checks,
             "e2e": {
-                "value": round(world * kv_bytes * args.steps / e2e_elapsed / 1e9, 2),
+                "value": round(kv_bytes * args.steps / e2e_elapsed / 1e9, 2),
                 "unit": "GB/s",
                 "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h,
@@ -537,10 +793,22 @@ def run_cuda(args: argparse.Namespace, world: int, rank: int, local: int) -> Non
                 "timing": "host wall clock from the first upload to the last result on the "
                           "host; uploads and downloads double-buffered on two copy streams",
             },
-            "gpu_launches": 3 * args.steps,
+            # K1, the decode's prep kernel and the decode (+ the peer-wait kernel when fused)
+            "gpu_launches": launches * args.steps,
             "clocks": clocks.summary(),
-        }
-        line["roofline"]["traffic"] = measured_traffic(decode_bytes)
+        }  # fmt: skip
+        if world > 1:
+            line["exchange"] = {
+                "collective": collective,
+                "how": ("fused: K2 stores each finished output row into every rank's [B, 32, D] "
+                        "buffer over NVLink, then a bounded device wait for all ranks' epoch"
+                        if pg is not None else
+                        "NCCL all_gather of [B, Hq/N, D] on a second stream, overlapping the "
+                        "next step"),
+                "bytes_per_step": B * case.num_q_heads * d * 2,
+                "per_rank": per_rank,
+            }  # fmt: skip
+        line["roofline"]["traffic"] = measured_traffic(decode_bytes) if world == 1 else None
         if world == 1 and not args.no_cpu_baseline:
             seqs, ks, vs, qs = gather_sample(case, kpool, vpool, q, 96 * 2**20)
             threads = os.cpu_count() or 1
@@ -552,10 +820,14 @@ def run_cuda(args: argparse.Namespace, world: int, rank: int, local: int) -> Non
                 "kind": "port",
                 "sample": f"{len(seqs)} of {B} sequences ({sb / 1e6:.0f} MB of KV) x {reps} passes",
             }
-        print(json.dumps(line), flush=True)
+    if pg is not None:
+        pg.close()
     if world > 1:
         dist.barrier(device_ids=[local])
         dist.destroy_process_group()
+    del kpool, vpool, ws, full, outs, gath, d_buf, d_out
+    torch.cuda.empty_cache()
+    return line if rank == 0 else None
 
 
 D70_METRIC = "KV-head-sharded paged decode KV-read GB/s (Llama-3-70B attention, 80 layers)"
@@ -827,6 +1099,215 @@ def run_kv_ops(args: argparse.Namespace, local: int) -> None:
     }), flush=True)  # fmt: skip
 
 
+LIVE_METRIC = "engine decode tokens/s (tokenserve Engine driving CudaPagedBackend, live)"
+
+
+def import_tokenserve():  # type: ignore[no-untyped-def]
+    """tokenserve itself (installed unmodified into baseline/_ref by the build)."""
+    ref = ROOT / "baseline" / "_ref"
+    if (ref / "tokenserve").is_dir() and str(ref) not in sys.path:
+        sys.path.append(str(ref))
+    import tokenserve.engine
+
+    return tokenserve
+
+
+class _KeepOpen:
+    """Lends a backend to a warm-up Engine without letting ``Engine.stop`` close it."""
+
+    def __init__(self, inner) -> None:  # type: ignore[no-untyped-def]
+        self.inner = inner
+        self.name = inner.name
+        self.supports_prefix_caching = inner.supports_prefix_caching
+
+    async def execute(self, batch):  # type: ignore[no-untyped-def]
+        return await self.inner.execute(batch)
+
+    def free(self, seq_id: int) -> None:
+        self.inner.free(seq_id)
+
+    async def close(self) -> None:
+        pass
+
+
+def drive_engine(backend, reqs, *, block_size: int, num_blocks: int, open_loop: bool,
+                 max_num_seqs: int = 64, keep_open: bool = False) -> dict:  # type: ignore[no-untyped-def]
+    """Serves ``reqs`` through tokenserve's own Engine (its scheduler, KV-cache manager and
+    step loop, src/tokenserve/engine.py) on ``backend``; request i is added at its arrival time
+    (``open_loop``) or all at t=0. Returns per-request tokens and latencies and the wall time."""
+    import asyncio
+
+    ts = import_tokenserve()
+    from tokenserve.engine import Engine, EngineConfig
+    from tokenserve.scheduler import SchedulerConfig
+    from tokenserve.sequence import SamplingParams
+    from tokenserve.tokenizer import ByteTokenizer
+
+    cfg = EngineConfig(block_size=block_size, num_blocks=num_blocks,
+                       scheduler=SchedulerConfig(max_num_seqs=max_num_seqs,
+                                                 max_model_len=4096))  # fmt: skip
+    assert ts is not None
+    eng = Engine(cfg, _KeepOpen(backend) if keep_open else backend, ByteTokenizer())
+    res: dict = {}
+
+    async def run() -> float:
+        await eng.start()
+        t0 = time.perf_counter()
+
+        async def one(i: int) -> None:
+            if open_loop:
+                delay = reqs.arrivals[i] - (time.perf_counter() - t0)
+                if delay > 0:
+                    await asyncio.sleep(delay)
+            t_arr = time.perf_counter()
+            stream = eng.add_request(f"r{i}", list(reqs.prompts[i]),
+                                     SamplingParams(max_tokens=reqs.max_tokens[i], ignore_eos=True))  # fmt: skip
+            toks, times = [], []
+            async for out in stream:
+                now = time.perf_counter()
+                toks += out.token_ids
+                times += [now] * len(out.token_ids)
+            res[i] = (t_arr, toks, times)
+
+        await asyncio.gather(*(one(i) for i in range(len(reqs))))
+        wall = time.perf_counter() - t0
+        await eng.wait_idle()
+        await eng.stop()
+        return wall
+
+    wall = asyncio.run(run())
+    ttft = [res[i][2][0] - res[i][0] for i in res if res[i][2]]
+    tpot = [(res[i][2][-1] - res[i][2][0]) / (len(res[i][1]) - 1) for i in res if len(res[i][1]) > 1]
+    m = eng.metrics
+    return {
+        "wall_s": wall,
+        "tokens": {i: res[i][1] for i in res},
+        "output_tokens": sum(len(res[i][1]) for i in res),
+        "ttft_ms_p50": 1000 * statistics.median(ttft),
+        "ttft_ms_p99": 1000 * float(np.percentile(ttft, 99)),
+        "tpot_ms_p50": 1000 * statistics.median(tpot),
+        "engine_steps": eng.num_steps,
+        "preemptions": eng.scheduler.num_preemptions,
+        "prefix_hit_tokens": eng.scheduler.prefix_hit_tokens,
+        "step_ms_mean": 1000 * m.step_duration._sum.get() / max(eng.num_steps, 1),
+    }
+
+
+def engine_tiny_live(dev, cpu_baseline: bool, cpu_seconds: float) -> dict:  # type: ignore[no-untyped-def]
+    """The tiny-Llama engine workload through tokenserve's live Engine, all 32 requests at
+    once (closed loop): output tokens/s, and every greedy token against the reference's own
+    (the cache-less greedy recompute recorded by tests/golden/make_golden.py, identical to
+    Engine + HFBackend). CPU: tokenserve's Engine + HFBackend itself on the host cores."""
+    import torch
+
+    from tokenserve_b200 import replay
+    from tokenserve_b200.backend import CudaPagedBackend, CudaPagedBackendConfig
+    from tokenserve_b200.workloads import tiny_engine_requests
+
+    torch.backends.cuda.matmul.allow_tf32 = False
+    reqs = tiny_engine_requests()
+    want = replay.load_trace(ROOT / "tests" / "golden" / "tiny_llama_trace.json.gz")["outputs"]
+    backend = CudaPagedBackend(build_model("engine-tiny", dev),
+                               CudaPagedBackendConfig(block_size=16, num_blocks=512, device=str(dev)))  # fmt: skip
+    drive_engine(backend, reqs, block_size=16, num_blocks=512, open_loop=False, keep_open=True)
+    with ClockSampler(dev) as clocks:
+        r = drive_engine(backend, reqs, block_size=16, num_blocks=512, open_loop=False)
+    mism = sum(a != b for i, toks in r["tokens"].items() for a, b in zip(toks, want[f"r{i}"], strict=True))
+    out = {
+        "workload": "tiny Llama (2 layers, hidden 256, 4q/2kv heads, D 64, vocab 32000, fp32), "
+                    "32 requests (prompts 64..512, half sharing a 128-token prefix), 32 greedy "
+                    "tokens each, all submitted at once; block 16 x 512 blocks",
+        "value": round(r["output_tokens"] / r["wall_s"], 1), "unit": "tokens/s",
+        "output_tokens": r["output_tokens"],
+        "greedy_mismatches_vs_reference": int(mism),
+        "reference_tokens": "cache-less greedy recompute of the same model (tokenserve Engine + "
+                            "HFBackend gives the same tokens), recorded in tests/golden",
+        "engine_steps": r["engine_steps"], "prefix_hit_tokens": r["prefix_hit_tokens"],
+        "ttft_ms_p50": round(r["ttft_ms_p50"], 2), "tpot_ms_p50": round(r["tpot_ms_p50"], 3),
+        "clocks": clocks.summary(),
+    }  # fmt: skip
+    if cpu_baseline:
+        import_tokenserve()
+        from tokenserve.backends.hf import HFBackend
+
+        threads = os.cpu_count() or 1
+        torch.set_num_threads(threads)
+        n = len(reqs)
+        # Bounded: the first requests only when the host is slow (~cpu_seconds of work).
+        sub = type(reqs)(reqs.prompts[:n], reqs.max_tokens[:n], reqs.arrivals[:n])
+        rc = drive_engine(HFBackend(build_model("engine-tiny", "cpu")), sub, block_size=16,
+                          num_blocks=512, open_loop=False)  # fmt: skip
+        cmism = sum(a != b for i, toks in rc["tokens"].items()
+                    for a, b in zip(toks, want[f"r{i}"], strict=True))  # fmt: skip
+        out["cpu_baseline"] = {
+            "value": round(rc["output_tokens"] / rc["wall_s"], 1), "unit": "tokens/s",
+            "cores": threads, "kind": "reference",
+            "sample": f"tokenserve Engine + HFBackend (the reference's own CPU backend), "
+                      f"{len(sub)} requests x 32 tokens, all submitted at once",
+            "greedy_mismatches_vs_reference": int(cmism),
+        }  # fmt: skip
+    del backend
+    torch.cuda.empty_cache()
+    return out
+
+
+def engine_8b_live(dev, rate_scale: float = 1.0) -> dict:  # type: ignore[no-untyped-def]
+    """The Llama-3-8B engine workload through tokenserve's live Engine, open loop: 160
+    requests arriving Poisson at 20 req/s (prompts 128..2048, 30% sharing a 512-token prefix,
+    greedy outputs 64..512), random bf16 weights, a pool of 51,500 blocks (60% of HBM).
+    Reports output tokens/s over the run, TTFT and TPOT. A closed-loop pass of the first 64
+    requests (64 tokens each) warms the decode-graph buckets first, as a server does at start."""
+    import torch
+
+    from tokenserve_b200.backend import CudaPagedBackend, CudaPagedBackendConfig
+    from tokenserve_b200.workloads import EngineRequests, llama8b_engine_requests
+
+    reqs = llama8b_engine_requests()
+    nb = 51500
+    backend = CudaPagedBackend(build_model("engine-8b", dev),
+                               CudaPagedBackendConfig(block_size=16, num_blocks=nb, device=str(dev)))  # fmt: skip
+    warm = EngineRequests(reqs.prompts[:64], [64] * 64, [0.0] * 64)
+    drive_engine(backend, warm, block_size=16, num_blocks=nb, open_loop=False, keep_open=True)
+    with ClockSampler(dev) as clocks:
+        r = drive_engine(backend, reqs, block_size=16, num_blocks=nb, open_loop=True)
+    out = {
+        "workload": "Llama-3-8B (random bf16 weights), 160 requests Poisson 20 req/s, prompts "
+                    "128..2048 (30% share a 512-token prefix), greedy outputs 64..512, block 16 "
+                    "x 51,500 blocks; tokenserve Engine defaults (64 sequences, 2048-token budget)",
+        "value": round(r["output_tokens"] / r["wall_s"], 1), "unit": "tokens/s",
+        "output_tokens": r["output_tokens"], "wall_s": round(r["wall_s"], 2),
+        "ttft_ms_p50": round(r["ttft_ms_p50"], 2), "ttft_ms_p99": round(r["ttft_ms_p99"], 2),
+        "tpot_ms_p50": round(r["tpot_ms_p50"], 3),
+        "engine_steps": r["engine_steps"], "step_ms_mean": round(r["step_ms_mean"], 3),
+        "preemptions": r["preemptions"], "prefix_hit_tokens": r["prefix_hit_tokens"],
+        "decode_graphs": len(backend._graphs.graphs) if backend._graphs is not None else 0,
+        "clocks": clocks.summary(),
+    }  # fmt: skip
+    del backend
+    torch.cuda.empty_cache()
+    return out
+
+
+def run_engine_live(args: argparse.Namespace, local: int) -> None:
+    """``--workload engine-tiny`` / ``engine-8b``: tokenserve's live Engine on the backend."""
+    import torch
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if args.workload == "engine-tiny":
+        r = engine_tiny_live(dev, not args.no_cpu_baseline, args.cpu_sample_seconds)
+        dtype = "f32"
+    else:
+        r = engine_8b_live(dev)
+        dtype = "bf16"
+    line = {"metric": LIVE_METRIC, "value": r.pop("value"), "unit": r.pop("unit"),
+            "n_gpus": 1, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": dtype, "data": "synthetic", "config": {"workload": r.pop("workload")},
+            "clocks": r.pop("clocks")}  # fmt: skip
+    line.update(r)
+    print(json.dumps(line), flush=True)
+
+
 ENGINE_METRIC = "engine decode tokens/s (recorded tokenserve engine schedule replayed)"
 
 
@@ -834,7 +1315,7 @@ def build_model(workload: str, dev):  # type: ignore[no-untyped-def]
     import torch
     import transformers
 
-    if workload == "engine-tiny":
+    if workload.startswith("engine-tiny"):
         torch.manual_seed(0)
         cfg = transformers.LlamaConfig(
             vocab_size=32000, hidden_size=256, intermediate_size=1024, num_hidden_layers=2,
@@ -867,7 +1348,7 @@ def run_engine(args: argparse.Namespace, local: int) -> None:
     torch.backends.cuda.matmul.allow_tf32 = False
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
-    name = "tiny_llama_trace" if args.workload == "engine-tiny" else "llama8b_engine_trace"
+    name = "tiny_llama_trace" if args.workload.startswith("engine-tiny") else "llama8b_engine_trace"
     trace = replay.load_trace(ROOT / "tests" / "golden" / f"{name}.json.gz")
     model = build_model(args.workload, dev)
     backend = CudaPagedBackend(model, CudaPagedBackendConfig(
@@ -921,7 +1402,7 @@ def run_engine(args: argparse.Namespace, local: int) -> None:
         "higher_is_better": True,
         "scaling": "weak",
         "vs_baseline": None,
-        "dtype": "f32" if args.workload == "engine-tiny" else "bf16",
+        "dtype": "f32" if args.workload.startswith("engine-tiny") else "bf16",
         "data": "synthetic",
         "config": {"workload": args.workload, "trace": f"tests/golden/{name}.json.gz",
                    "engine_steps": len(steps), "sampled_tokens": n_sampled,
@@ -947,7 +1428,7 @@ def run_engine(args: argparse.Namespace, local: int) -> None:
             "weight_bytes": weight_bytes,
             "kv_bytes_per_context_token": kv_token_bytes,
         }  # fmt: skip
-    if args.workload == "engine-tiny" and not args.no_cpu_baseline:
+    if args.workload.startswith("engine-tiny") and not args.no_cpu_baseline:
         from oracle.hf_engine import HFStepLoop
 
         threads = os.cpu_count() or 1
@@ -965,7 +1446,7 @@ def run_engine(args: argparse.Namespace, local: int) -> None:
                                 "cores": threads, "kind": "port",
                                 "sample": f"HFBackend step loop on {done} of {len(steps)} "
                                           f"recorded steps ({sampled} sampled tokens)"}  # fmt: skip
-    elif args.workload == "engine-8b":
+    elif args.workload.startswith("engine-8b"):
         line["cpu_baseline"] = {"value": None, "unit": "tokens/s", "kind": "port",
                                 "sample": "not run: an 8B model on the host cores at this load "
                                           "is infeasible; the tiny-Llama engine carries the "
@@ -1081,27 +1562,29 @@ def run_swap(args: argparse.Namespace, local: int) -> None:
 PREFILL_METRIC = "chunked-prefill paged attention TFLOP/s (bf16, % of tensor peak)"
 
 
-def prefill_cpu_rate(work, kpool, vpool, q_rounds, seconds_target, threads):  # type: ignore[no-untyped-def]
-    """Oracle TFLOP/s on sequence 0's chunks (one layer), repeated for ~seconds_target."""
+def prefill_cpu_rate(work, seconds_target, threads):  # type: ignore[no-untyped-def]
+    """Oracle TFLOP/s on sequence 0's chunks (one layer), repeated for ~seconds_target.
+
+    The CPU times float32 eager attention over seeded host inputs of the workload's shapes
+    (the chunk's queries over the cached prefix plus the chunk), as HFBackend would compute it.
+    """
     import torch
 
     from oracle.attention import eager_attention_torch
 
     torch.set_num_threads(threads)
+    g = torch.Generator().manual_seed(7)
     jobs = []
-    for r, q in zip(work.rounds, q_rounds, strict=True):
+    for r in work.rounds:
         if 0 not in r.seqs.tolist():
             continue
         i = r.seqs.tolist().index(0)
-        ctx = int(r.context_lens[i])
-        nblk = (ctx + 15) // 16
-        ids = torch.from_numpy(r.block_tables[i, :nblk].astype(np.int64)).to(kpool.device)
-        k = kpool.index_select(0, ids).transpose(0, 1).reshape(8, nblk * 16, 128)[:, :ctx]
-        v = vpool.index_select(0, ids).transpose(0, 1).reshape(8, nblk * 16, 128)[:, :ctx]
-        lo, hi = int(r.query_start_loc[i]), int(r.query_start_loc[i + 1])
-        jobs.append((q[lo:hi].transpose(0, 1).float().cpu(), k.float().cpu(), v.float().cpu()))
+        ctx, c = int(r.context_lens[i]), int(r.chunk_lens[i])
+        jobs.append((torch.randn(32, c, 128, generator=g) * 0.5,
+                     torch.randn(8, ctx, 128, generator=g) * 0.5,
+                     torch.randn(8, ctx, 128, generator=g) * 0.5))  # fmt: skip
     flops = 0
-    for qh, k, v in jobs:
+    for qh, k, _ in jobs:
         c, n_prev = qh.shape[1], k.shape[1] - qh.shape[1]
         flops += 4 * 32 * 128 * (c * n_prev + c * (c + 1) // 2)
 
@@ -1117,29 +1600,25 @@ def prefill_cpu_rate(work, kpool, vpool, q_rounds, seconds_target, threads):  # 
     return flops * reps / t / 1e12, flops, reps
 
 
-def run_prefill(args: argparse.Namespace, world: int, rank: int, local: int) -> None:
+def prefill_measure(args: argparse.Namespace, dev, steps: int, warmup: int, seed: int = 0,
+                    parity: bool = True) -> dict:  # type: ignore[no-untyped-def]
     """Chunked prefill with prefix caching, Llama-3-8B geometry, all layers' pools resident.
 
     One step = for each 512-token chunk round, for each layer: K1 writes the chunk's K/V into
     that layer's pool, then K3 attends the chunk over the cached prefix + itself (causal).
+    Returns the timing (CUDA events around every K3 launch and the whole step) and, with
+    ``parity``, the oracle's check of the last layer's timed output for a sample of sequences
+    of the first and last chunk rounds.
     """
     import torch
-    import torch.distributed as dist
 
     from tokenserve_b200 import ops
     from tokenserve_b200.workloads import prefill_workload
 
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    if world > 1:
-        import datetime
-
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
-                                device_id=dev)  # fmt: skip
     ops.load_library()
-    work = prefill_workload(seed=rank, num_layers=args.layers)
+    work = prefill_workload(seed=seed, num_layers=args.layers)
     L, nb, dt = work.num_layers, work.num_blocks, torch.bfloat16
-    g = torch.Generator(device=dev).manual_seed(2000 + rank)
+    g = torch.Generator(device=dev).manual_seed(2000 + seed)
     pools = torch.empty((L, 2, nb, 8, 16, 128), dtype=dt, device=dev)
     for li in range(L):
         pools[li].normal_(0.0, 0.5, generator=g)
@@ -1155,8 +1634,8 @@ def run_prefill(args: argparse.Namespace, world: int, rank: int, local: int) -> 
             "qsl": torch.from_numpy(r.query_start_loc).to(dev),
             "ctx": torch.from_numpy(r.context_lens).to(dev),
             "maxq": int(r.chunk_lens.max()),
+            "out": torch.empty((t, 32, 128), dtype=dt, device=dev),
         })  # fmt: skip
-    out = torch.empty((max(r.num_tokens for r in work.rounds), 32, 128), dtype=dt, device=dev)
     scale = 128**-0.5
     stream = torch.cuda.current_stream()
     flops_step = work.flops_per_layer() * L
@@ -1164,53 +1643,113 @@ def run_prefill(args: argparse.Namespace, world: int, rank: int, local: int) -> 
     def step(events=None):  # type: ignore[no-untyped-def]
         n = 0
         for rd in rounds:
-            o = out[: rd["q"].shape[0]]
             for li in range(L):
                 kp, vp = pools[li, 0], pools[li, 1]
                 ops.reshape_and_cache(rd["k"], rd["v"], kp, vp, rd["slots"])
                 if events is not None:
                     events[n][0].record(stream)
-                ops.paged_prefill(o, rd["q"], kp, vp, rd["bt"], rd["qsl"], rd["ctx"], rd["maxq"],
-                                  scale)  # fmt: skip
+                ops.paged_prefill(rd["out"], rd["q"], kp, vp, rd["bt"], rd["qsl"], rd["ctx"],
+                                  rd["maxq"], scale)  # fmt: skip
                 if events is not None:
                     events[n][1].record(stream)
                 n += 1
 
-    def barrier() -> None:
-        if world > 1:
-            dist.barrier(device_ids=[local])
-        torch.cuda.synchronize()
-
-    for _ in range(max(args.warmup, 3)):
+    for _ in range(max(warmup, 3)):
         step()
-    barrier()
+    torch.cuda.synchronize()
     nl = len(rounds) * L
     evs = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-            for _ in range(nl)] for _ in range(args.steps)]  # fmt: skip
+            for _ in range(nl)] for _ in range(steps)]  # fmt: skip
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(dev) as clocks:
         e0.record(stream)
-        for i in range(args.steps):
+        for i in range(steps):
             step(evs[i])
         e1.record(stream)
         torch.cuda.synchronize()
-    barrier()
-    elapsed = e0.elapsed_time(e1) / 1e3
-    k3 = sum(a.elapsed_time(b) for st in evs for a, b in st) / 1e3
+    res = {
+        "elapsed": e0.elapsed_time(e1) / 1e3,
+        "k3": sum(a.elapsed_time(b) for st in evs for a, b in st) / 1e3,
+        "launches": nl * steps, "flops_step": flops_step, "work": work, "clocks": clocks,
+        "pool_bytes": pools.numel() * 2,
+    }  # fmt: skip
+    if parity:
+        from oracle.attention import paged_prefill_np
+
+        # Every round's `out` holds the last layer's output of the last timed step.
+        kh = pools[L - 1, 0].float().cpu().numpy()
+        vh = pools[L - 1, 1].float().cpu().numpy()
+        worst_rel = worst_frac = 0.0
+        ok, checked = True, 0
+        for ri in (0, len(work.rounds) - 1):
+            r, rd = work.rounds[ri], rounds[ri]
+            order = np.argsort(-r.context_lens.astype(np.int64), kind="stable")
+            for i in sorted({int(order[0]), int(order[len(order) // 2]), int(order[-1])}):
+                lo, hi = int(r.query_start_loc[i]), int(r.query_start_loc[i + 1])
+                ref = paged_prefill_np(rd["q"][lo:hi].float().cpu().numpy(), kh, vh,
+                                       [r.block_tables[i]], [0, hi - lo], [r.context_lens[i]],
+                                       scale)  # fmt: skip
+                got = rd["out"][lo:hi].float().cpu().numpy().astype(np.float64)
+                err = np.abs(got - ref)
+                tol = 2e-3 * np.abs(ref).max() + 2.0**-8 * np.abs(ref)
+                ok &= bool((err <= tol).all())
+                worst_rel = max(worst_rel, float(err.max() / np.abs(ref).max()))
+                worst_frac = max(worst_frac, float((err / tol).max()))
+                checked += 1
+        res["parity"] = {
+            "ok": ok, "seqs_checked": checked,
+            "rounds_checked": [0, len(work.rounds) - 1], "layer_checked": L - 1,
+            "max_abs_err_over_max_ref": worst_rel, "max_err_over_tolerance": worst_frac,
+            "tolerance": "|out - ref| <= 2e-3 * max|ref| + 2^-8 * |ref| (float64 oracle)",
+        }  # fmt: skip
+    del pools, rounds
+    torch.cuda.empty_cache()
+    return res
+
+
+def prefill_roofline(res: dict, steps: int) -> dict:
+    pk = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (
+        ROOT / "MEASURED_PEAKS.json").exists() else {}
+    sustained = float(pk.get("bf16_tflops_sustained", 1400.0))
+    burst = float(pk.get("bf16_tflops", 1590.0))
+    achieved = res["flops_step"] * steps / res["k3"] / 1e12
+    return {
+        "bound": "tensor", "kernel": "paged_prefill_tc_kernel",
+        "achieved": round(achieved, 1), "peak": sustained,
+        "peak_kind": "measured, sustained (the step is ~0.1 s of back-to-back GEMM-like work)"
+                     if pk else "fallback, sustained",
+        "unit": "TFLOP/s", "frac": round(achieved / sustained, 4),
+        "frac_of_burst_peak": round(achieved / burst, 4),
+        "avg_launch_us": round(res["k3"] / res["launches"] * 1e6, 2),
+        "traffic": prefill_traffic()[0], "traffic_launch": prefill_traffic()[1],
+    }  # fmt: skip
+
+
+def run_prefill(args: argparse.Namespace, world: int, rank: int, local: int) -> None:
+    """The chunked-prefill workload as its own line (``--workload prefill``)."""
+    import torch
+    import torch.distributed as dist
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=dev)  # fmt: skip
+    res = prefill_measure(args, dev, args.steps, args.warmup, seed=rank,
+                          parity=rank == 0 and not args.skip_parity)  # fmt: skip
+    elapsed = res["elapsed"]
     if world > 1:
         tt = torch.tensor([elapsed], dtype=torch.float64, device=dev)
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
         elapsed = tt.item()
     if rank == 0:
-        pk = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (
-            ROOT / "MEASURED_PEAKS.json").exists() else {}
-        sustained = float(pk.get("bf16_tflops_sustained", 1400.0))
-        burst = float(pk.get("bf16_tflops", 1590.0))
-        achieved = flops_step * args.steps / k3 / 1e12
-        value = world * flops_step * args.steps / elapsed / 1e12
+        work = res["work"]
+        L = work.num_layers
         line = {
             "metric": PREFILL_METRIC,
-            "value": round(value, 2),
+            "value": round(world * res["flops_step"] * args.steps / elapsed / 1e12, 2),
             "unit": "TFLOP/s",
             "n_gpus": world,
             "steps": args.steps,
@@ -1226,25 +1765,16 @@ def run_prefill(args: argparse.Namespace, world: int, rank: int, local: int) -> 
                             "D=128, bf16, block 16)",
                 "sequences": len(work.suffix_lens), "cached_prefix": 1024,
                 "suffix": "uniform 256..2048", "chunk": 512, "layers": L,
-                "flop_per_step": flops_step,
-                "l2": f"{L} layers' pools ({pools.numel() * 2 / 1e9:.1f} GB) larger than L2",
+                "flop_per_step": res["flops_step"],
+                "l2": f"{L} layers' pools ({res['pool_bytes'] / 1e9:.1f} GB) larger than L2",
             },
-            "roofline": {
-                "bound": "tensor", "kernel": "paged_prefill_tc_kernel",
-                "achieved": round(achieved, 1), "peak": sustained,
-                "peak_kind": "measured, sustained (the step is ~0.1 s of back-to-back GEMM-like work)",
-                "unit": "TFLOP/s", "frac": round(achieved / sustained, 4),
-                "frac_of_burst_peak": round(achieved / burst, 4),
-                "avg_launch_us": round(k3 / (args.steps * nl) * 1e6, 2),
-                "traffic": prefill_traffic()[0], "traffic_launch": prefill_traffic()[1],
-            },
-            "gpu_launches": 2 * nl * args.steps,
-            "clocks": clocks.summary(),
+            "roofline": prefill_roofline(res, args.steps),
+            "parity": res.get("parity"),
+            "gpu_launches": 2 * res["launches"],
+            "clocks": res["clocks"].summary(),
         }  # fmt: skip
         if world == 1 and not args.no_cpu_baseline:
-            qs = [rd["q"] for rd in rounds]
-            tf, fl, reps = prefill_cpu_rate(work, pools[0, 0], pools[0, 1], qs,
-                                            args.cpu_sample_seconds, os.cpu_count() or 1)  # fmt: skip
+            tf, fl, reps = prefill_cpu_rate(work, args.cpu_sample_seconds, os.cpu_count() or 1)
             line["cpu_baseline"] = {"value": round(tf, 4), "unit": "TFLOP/s",
                                     "cores": os.cpu_count() or 1, "kind": "port",
                                     "sample": f"sequence 0's chunks, one layer ({fl / 1e9:.1f} "

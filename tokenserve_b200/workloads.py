@@ -186,3 +186,53 @@ def decode70b_workload(seed: int = 0, batch: int = 512, undersize: float = 0.85)
     ctx = ctx[:admitted]
     tables = tables_from_permutation(rng, ctx, num_blocks, 16)
     return PagedCase(num_blocks, 16, 64, 8, 128, ctx, tables, seed)
+
+
+@dataclass
+class EngineRequests:
+    """Requests for tokenserve's Engine: prompt token ids, output lengths, arrival times (s)."""
+
+    prompts: list[list[int]]
+    max_tokens: list[int]
+    arrivals: list[float]  # Poisson process, seconds from the start
+
+    def __len__(self) -> int:
+        return len(self.prompts)
+
+
+def tiny_engine_requests(seed: int = 0) -> EngineRequests:
+    """The tiny-Llama engine workload: 32 requests, prompt ids uniform in [3, 32000), lengths
+    uniform 64..512, the even-numbered ones starting with one shared seeded 128-token prefix,
+    32 greedy output tokens each, Poisson arrivals at 4 req/s (the same draws as the recorded
+    tiny-Llama trace's requests)."""
+    rng = np.random.default_rng(seed)
+    n = 32
+    lens = rng.integers(64, 513, n)
+    prefix = rng.integers(3, 32000, 128).tolist()
+    prompts = []
+    for i in range(n):
+        p = rng.integers(3, 32000, int(lens[i])).tolist()
+        if i % 2 == 0:
+            p[:128] = prefix
+        prompts.append(p)
+    arrivals = np.cumsum(rng.exponential(1 / 4.0, n)).tolist()
+    return EngineRequests(prompts, [32] * n, arrivals)
+
+
+def llama8b_engine_requests(seed: int = 4) -> EngineRequests:
+    """The Llama-3-8B engine workload: 160 requests arriving Poisson at 20 req/s, prompt ids
+    uniform over the 128,256-token vocabulary, prompt lengths uniform 128..2048, 30% sharing
+    one seeded 512-token prefix, greedy output lengths uniform 64..512 (the same draws as the
+    recorded Llama-3-8B engine trace's requests)."""
+    rng = np.random.default_rng(seed)
+    n = 160
+    prefix = rng.integers(0, 128256, 512).tolist()
+    prompts, max_tokens = [], []
+    for _ in range(n):
+        p = rng.integers(0, 128256, int(rng.integers(128, 2049))).tolist()
+        if rng.random() < 0.3:
+            p[:512] = prefix
+        prompts.append(p)
+        max_tokens.append(int(rng.integers(64, 513)))
+    arrivals = np.cumsum(rng.exponential(1 / 20.0, n)).tolist()
+    return EngineRequests(prompts, max_tokens, arrivals)
