@@ -1143,7 +1143,10 @@ def drive_engine(backend, reqs, *, block_size: int, num_blocks: int, open_loop: 
     from tokenserve.sequence import SamplingParams
     from tokenserve.tokenizer import ByteTokenizer
 
-    cfg = EngineConfig(block_size=block_size, num_blocks=num_blocks,
+    # Every request is queued at once in the closed-loop runs: the waiting-queue limits
+    # (back-pressure, engine.py:236-245) are lifted as tokenserve's own tests do.
+    cfg = EngineConfig(block_size=block_size, num_blocks=num_blocks, max_waiting_seqs=100_000,
+                       max_waiting_tokens=100_000_000,
                        scheduler=SchedulerConfig(max_num_seqs=max_num_seqs,
                                                  max_model_len=4096))  # fmt: skip
     assert ts is not None

@@ -78,7 +78,10 @@ def test_live_engine_tiny_llama_greedy_matches_reference(cuda_device, num_blocks
     reqs = tiny_engine_requests()
     backend = CudaPagedBackend(model, CudaPagedBackendConfig(block_size=16, num_blocks=num_blocks,
                                                              device=str(cuda_device)))  # fmt: skip
-    eng = Engine(EngineConfig(block_size=16, num_blocks=num_blocks), backend, TOK)
+    # All 32 requests are queued at once: lift the waiting-queue limits, as tokenserve's own
+    # tests do (their default is one pool's worth of prompt tokens).
+    eng = Engine(EngineConfig(block_size=16, num_blocks=num_blocks, max_waiting_seqs=1000,
+                              max_waiting_tokens=1_000_000), backend, TOK)  # fmt: skip
     assert eng.kv.enable_prefix_caching  # the CUDA backend shares KV; the engine keeps caching on
 
     async def run() -> list:

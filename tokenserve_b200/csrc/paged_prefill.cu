@@ -16,8 +16,9 @@
 //     3-stage K ring and a 2-stage V ring: a K stage is released after the last QK that reads it,
 //     a V stage after the last PV, so K loads run further ahead.
 //   * warp 9 (one lane): tcgen05.mma S_x = Q_x K^T (M=N=K=128, both K-major) into tile x's TMEM
-//     S, then O_x += P_x V with P read from TMEM (bf16, written over S) and V MN-major, in the
-//     order PV_A(j), QK_A(j+1), PV_B(j), QK_B(j+1): one tile's softmax overlaps the other's MMAs.
+//     S, then O_x += P_x V with P read from TMEM (written over S as two half-precision parts,
+//     P_hi + P_lo, so the product keeps ~16 bits of P) and V MN-major, in the order PV_A(j),
+//     QK_A(j+1), PV_B(j), QK_B(j+1): one tile's softmax overlaps the other's MMAs.
 //   * warps 0-3 / 4-7 (one warpgroup per query tile, thread = row = TMEM lane): online softmax
 //     in fp32 (exp2 domain, causal mask only on diagonal tiles, stale max kept unless exceeded by
 //     2^8 so O is rarely rescaled), P back to TMEM, O rescale in TMEM, and the epilogue.
@@ -279,10 +280,14 @@ __global__ void __maxnreg__(kMaxRegs)
           }
           ts::tc::fence_after_sync();
           const uint64_t dv = dv0 + uint64_t((st * kTileBytes) >> 4);
+          // O_x += P_hi V + P_lo V (P_hi in S columns [0, 64), P_lo in [64, 128)).
 #pragma unroll
-          for (int kk = 0; kk < 8; ++kk)
-            ts::tc::mma_ts(tmem + 256 + x * 128, tmem + x * 128 + kk * 8,
-                           dv + uint64_t((kk * 2048) >> 4), idesc_pv, j > 0 || kk > 0);
+          for (int part = 0; part < 2; ++part)
+#pragma unroll
+            for (int kk = 0; kk < 8; ++kk)
+              ts::tc::mma_ts(tmem + 256 + x * 128, tmem + x * 128 + part * 64 + kk * 8,
+                             dv + uint64_t((kk * 2048) >> 4), idesc_pv,
+                             j > 0 || part > 0 || kk > 0);
           ts::tc::commit(&bars->pv_done[x]);
           if (x == last_user(j) && j + kVStages < n_max) ts::tc::commit(&bars->v_empty[st]);
           last_pv[x] = j;
@@ -335,8 +340,12 @@ __global__ void __maxnreg__(kMaxRegs)
             if (c > limit) sr[c] = __float_as_uint(-INFINITY);
         }
       };
-      // P = exp2(s * scale - m_run) packed to half precision pairs in place (over S), with
-      // the row sum and the largest exponent seen (xm), which the exponentials do not wait on.
+      // P = exp2(s * scale - m_run) as two half-precision parts, P = P_hi + P_lo with
+      // P_lo = round(P - P_hi): the PV product then keeps ~16 mantissa bits of P instead of 8
+      // (a bf16 P alone leaves errors near 2e-3 of max|O| at 1,536-token contexts). Registers
+      // sr[c..c+3] of the four scores just read take P_hi of (c, c+1), (c+2, c+3) and then
+      // P_lo of the same pairs. Also the row sum and the largest exponent seen (xm), which
+      // the exponentials do not wait on.
       float sum0, sum1, xm;
       auto exp_pass = [&]() {
         sum0 = 0.f;
@@ -353,8 +362,12 @@ __global__ void __maxnreg__(kMaxRegs)
           const float p0 = ex2(x0), p1 = ex2(x1), p2 = ex2(x2), p3 = ex2(x3);
           sum0 += p0 + p2;
           sum1 += p1 + p3;
-          sr[c / 2] = Mma::pack(p0, p1);
-          sr[c / 2 + 1] = Mma::pack(p2, p3);
+          const uint32_t h01 = Mma::pack(p0, p1), h23 = Mma::pack(p2, p3);
+          const float2 f01 = Mma::unpack(h01), f23 = Mma::unpack(h23);
+          sr[c] = h01;
+          sr[c + 1] = h23;
+          sr[c + 2] = Mma::pack(p0 - f01.x, p1 - f01.y);
+          sr[c + 3] = Mma::pack(p2 - f23.x, p3 - f23.y);
         }
         xm = fmaxf(xa, xb);
       };
@@ -379,9 +392,14 @@ __global__ void __maxnreg__(kMaxRegs)
         }
         exp_pass();
       }
+      // P_hi over S columns [0, 64), P_lo over [64, 128): word w of part k (pair w of the row)
+      // sits in sr[4 * (w / 2) + 2 * k + w % 2].
 #pragma unroll
-      for (int c2 = 0; c2 < 2; ++c2) {
-        uint32_t (&chunk)[32] = *reinterpret_cast<uint32_t(*)[32]>(sr + 32 * c2);
+      for (int c2 = 0; c2 < 4; ++c2) {
+        const int part = c2 / 2, w0 = (c2 % 2) * 32;
+        uint32_t chunk[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) chunk[i] = sr[4 * ((w0 + i) / 2) + 2 * part + (w0 + i) % 2];
         ts::tc::tmem_st32(lane_base + s_col + c2 * 32, chunk);
       }
       ts::tc::wait_st();
