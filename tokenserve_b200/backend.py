@@ -28,6 +28,7 @@ import torch
 from tokenserve_b200 import ops
 from tokenserve_b200.interface import Backend, BatchItem, KVCorruptionError
 from tokenserve_b200.model import DecodeGraphs, PagedLlamaRunner
+from tokenserve_b200.sharding import shard_heads
 from tokenserve_b200.step import plan_decode, plan_step
 
 
@@ -48,6 +49,11 @@ class CudaPagedBackendConfig:
     #: Blocks of pinned host memory for swap-to-host preemption (:meth:`CudaPagedBackend.swap_out`);
     #: 0 = no swap space. A block holds every layer's K and V for ``block_size`` tokens.
     swap_space_blocks: int = 0
+    #: Ranks the model's KV heads are split over (one process per GPU, ``torch.distributed``
+    #: initialised; every rank runs the same engine and gets the same batches). Rank r holds KV
+    #: heads [r * Hkv / N, (r + 1) * Hkv / N) and their query heads in a pool of Hkv / N heads;
+    #: each layer's attention output is all-gathered (NCCL) before the O projection.
+    kv_head_shards: int = 1
 
     def __post_init__(self) -> None:
         if self.block_size <= 0 or self.num_blocks <= 0:
@@ -78,7 +84,8 @@ class CudaPagedBackend(Backend):
     name = "cuda-paged"
     supports_prefix_caching = True
 
-    def __init__(self, model: torch.nn.Module, config: CudaPagedBackendConfig) -> None:
+    def __init__(self, model: torch.nn.Module, config: CudaPagedBackendConfig,
+                 group=None) -> None:  # type: ignore[no-untyped-def]  # fmt: skip
         if not torch.cuda.is_available():
             raise RuntimeError("CudaPagedBackend needs a CUDA device (there is no CPU fallback)")
         ops.load_library()
@@ -86,6 +93,17 @@ class CudaPagedBackend(Backend):
         self.device = torch.device(config.device)
         if self.device.index is None:
             self.device = torch.device("cuda", torch.cuda.current_device())
+        shard = None
+        if config.kv_head_shards > 1:
+            import torch.distributed as dist
+
+            if not dist.is_initialized() or dist.get_world_size(group) != config.kv_head_shards:
+                raise ValueError(f"kv_head_shards={config.kv_head_shards} needs a process group "
+                                 "of that many ranks")  # fmt: skip
+            mc = model.config
+            shard = shard_heads(mc.num_attention_heads, mc.num_key_value_heads,
+                                config.kv_head_shards, dist.get_rank(group))  # fmt: skip
+        self.shard = shard
         with torch.cuda.device(self.device):
             self.runner = PagedLlamaRunner(
                 model,
@@ -93,6 +111,8 @@ class CudaPagedBackend(Backend):
                 block_size=config.block_size,
                 device=self.device,
                 dtype=config.dtype,
+                shard=shard,
+                group=group,
             )
             self._tags = (
                 torch.full((config.num_blocks * config.block_size,), -1, dtype=torch.int32,
@@ -100,7 +120,10 @@ class CudaPagedBackend(Backend):
                 if config.verify_kv else None
             )  # fmt: skip
             self.runner.tag_pool = self._tags
-        self._graphs = DecodeGraphs(self.runner) if config.cuda_graphs and not config.verify_kv else None
+        # Decode steps replay as CUDA graphs on one GPU; a sharded step (its per-layer NCCL
+        # all-gather) runs eagerly.
+        self._graphs = (DecodeGraphs(self.runner)
+                        if config.cuda_graphs and not config.verify_kv and shard is None else None)  # fmt: skip
         r = self.runner
         #: pinned host arena [layers * 2][swap blocks][block plane] (same plane layout as the pool)
         self.swap_space = (
@@ -172,7 +195,7 @@ class CudaPagedBackend(Backend):
                                         dtype=torch.int32, device=self.device)  # fmt: skip
                 self.runner.tag_pool = self._tags
         self.config = dataclasses.replace(self.config, num_blocks=num_blocks)
-        if self.config.cuda_graphs and not self.config.verify_kv:
+        if self.config.cuda_graphs and not self.config.verify_kv and self.shard is None:
             self._graphs = DecodeGraphs(self.runner)
 
     @property

@@ -17,6 +17,7 @@ import numpy as np
 import torch
 
 from tokenserve_b200 import ops
+from tokenserve_b200.sharding import HeadShard, gather_heads, heads_from_gathered, shard_qkv_weight
 from tokenserve_b200.step import BlockTableMirror, DecodePlan, StepPlan
 
 
@@ -77,7 +78,15 @@ class Staging:
 
 
 class PagedLlamaRunner:
-    """Runs steps of a ``LlamaForCausalLM`` against a device-resident paged KV pool."""
+    """Runs steps of a ``LlamaForCausalLM`` against a device-resident paged KV pool.
+
+    With a :class:`~tokenserve_b200.sharding.HeadShard` the runner is one rank of a KV-head
+    split: it projects, caches and attends only its KV heads and their query heads (its slices
+    of the Q/K/V weights, a pool of ``Hkv/N`` heads), all-gathers each layer's attention output
+    ``[T, Hq/N, D]`` over ``group`` into ``[T, Hq, D]`` in model head order, and runs the rest of
+    the layer (O projection, MLP, norms, lm_head) on every rank, so every rank ends each step
+    with the same logits.
+    """
 
     def __init__(
         self,
@@ -87,6 +96,8 @@ class PagedLlamaRunner:
         block_size: int,
         device: torch.device | str = "cuda",
         dtype: torch.dtype | None = None,
+        shard: HeadShard | None = None,
+        group=None,  # type: ignore[no-untyped-def]
     ) -> None:
         self.device = torch.device(device)
         self.model = model.to(self.device).eval()
@@ -95,8 +106,12 @@ class PagedLlamaRunner:
         if self.dtype != next(model.parameters()).dtype:
             self.model = self.model.to(self.dtype)
         self.num_layers = cfg.num_hidden_layers
-        self.num_q_heads = cfg.num_attention_heads
-        self.num_kv_heads = cfg.num_key_value_heads
+        self.total_q_heads = cfg.num_attention_heads
+        self.shard = shard
+        self.group = group
+        # Heads this runner attends (all of them, or its shard's).
+        self.num_q_heads = shard.num_q_heads if shard else cfg.num_attention_heads
+        self.num_kv_heads = shard.num_kv_heads if shard else cfg.num_key_value_heads
         self.head_dim = getattr(cfg, "head_dim", None) or cfg.hidden_size // cfg.num_attention_heads
         self.scale = self.head_dim**-0.5
         self.block_size = block_size
@@ -114,6 +129,9 @@ class PagedLlamaRunner:
         #: int32 [num_blocks * block_size] token id per slot, or None (shadow-KV check off)
         self.tag_pool: torch.Tensor | None = None
         self.fused = self._fuse_weights()
+        if shard is not None and not self.fused:
+            raise NotImplementedError("KV-head sharding covers bias-free Llama layers with default "
+                                      "RoPE and SiLU (the fused path)")  # fmt: skip
 
     @property
     def block_bytes(self) -> int:
@@ -144,15 +162,21 @@ class PagedLlamaRunner:
                 or getattr(self.rotary, "attention_scaling", 1.0) != 1.0):  # fmt: skip
             return False
         self._w_qkv, self._w_gu = [], []
+        d, sh = self.head_dim, self.shard
         with torch.no_grad():
             for layer in self.base.layers:
                 at, mlp = layer.self_attn, layer.mlp
-                w = torch.cat([at.q_proj.weight, at.k_proj.weight, at.v_proj.weight]).contiguous()
-                a, b = at.q_proj.weight.shape[0], at.k_proj.weight.shape[0]
-                at.q_proj.weight.data = w[:a]
-                at.k_proj.weight.data = w[a : a + b]
-                at.v_proj.weight.data = w[a + b :]
-                self._w_qkv.append(w)
+                if sh is not None:
+                    # This rank's rows only: its query heads' Q rows, its KV heads' K and V rows.
+                    self._w_qkv.append(shard_qkv_weight(at.q_proj.weight, at.k_proj.weight,
+                                                        at.v_proj.weight, sh, d))  # fmt: skip
+                else:
+                    w = torch.cat([at.q_proj.weight, at.k_proj.weight, at.v_proj.weight]).contiguous()
+                    a, b = at.q_proj.weight.shape[0], at.k_proj.weight.shape[0]
+                    at.q_proj.weight.data = w[:a]
+                    at.k_proj.weight.data = w[a : a + b]
+                    at.v_proj.weight.data = w[a + b :]
+                    self._w_qkv.append(w)
                 g = torch.cat([mlp.gate_proj.weight, mlp.up_proj.weight]).contiguous()
                 i = mlp.gate_proj.weight.shape[0]
                 mlp.gate_proj.weight.data = g[:i]
@@ -215,6 +239,12 @@ class PagedLlamaRunner:
                               st.prefill_ctx, st.max_query_len, self.scale)  # fmt: skip
         return out
 
+    def gather_heads(self, o: torch.Tensor) -> torch.Tensor:
+        """``[T, Hq/N, D]`` of this rank -> ``[T, Hq, D]`` of all ranks (identity unsharded)."""
+        if self.shard is None:
+            return o
+        return heads_from_gathered(gather_heads(o, group=self.group))
+
     @torch.inference_mode()
     def forward(self, st: DeviceStep, float_logits: bool = True) -> torch.Tensor:
         """Runs every layer over the step's tokens; returns the logits of the sampled rows, in
@@ -239,8 +269,8 @@ class PagedLlamaRunner:
             q = torch.empty((t, hq, d), dtype=res.dtype, device=res.device)
             ops.rope_and_cache(qkv, q, self.kv[li, 0], self.kv[li, 1], st.slot_mapping,
                                st.positions, self._inv_freq, hq, hkv)  # fmt: skip
-            o = self.attend(li, q, st)
-            a = at.o_proj(o.view(t, hq * d))
+            o = self.gather_heads(self.attend(li, q, st))
+            a = at.o_proj(o.view(t, self.total_q_heads * d))
             x2 = torch.empty_like(res)
             ops.add_rmsnorm(x2, res, a, layer.post_attention_layernorm.weight, self._eps[li][1])
             gu = f.linear(x2, self._w_gu[li])
@@ -260,14 +290,19 @@ class PagedLlamaRunner:
         cos, sin = cos[0], sin[0]
         t = h.shape[0]
         hq, hkv, d = self.num_q_heads, self.num_kv_heads, self.head_dim
+        f = torch.nn.functional
         for li, layer in enumerate(self.base.layers):
             attn = layer.self_attn
             x = layer.input_layernorm(h)
-            q = _rope(attn.q_proj(x).view(t, hq, d), cos, sin)
-            k = _rope(attn.k_proj(x).view(t, hkv, d), cos, sin)
-            v = attn.v_proj(x).view(t, hkv, d)
-            o = self.attention(li, q, k, v, st)
-            h = h + attn.o_proj(o.view(t, hq * d))
+            if self.shard is None:
+                qp, kp, vp = attn.q_proj(x), attn.k_proj(x), attn.v_proj(x)
+            else:
+                qp, kp, vp = f.linear(x, self._w_qkv[li]).split([hq * d, hkv * d, hkv * d], 1)
+            q = _rope(qp.reshape(t, hq, d), cos, sin)
+            k = _rope(kp.reshape(t, hkv, d), cos, sin)
+            v = vp.reshape(t, hkv, d)
+            o = self.gather_heads(self.attention(li, q, k, v, st))
+            h = h + attn.o_proj(o.reshape(t, self.total_q_heads * d))
             h = h + layer.mlp(layer.post_attention_layernorm(h))
         hs = self.base.norm(h[st.sample_rows])
         return self.model.lm_head(hs)

@@ -51,6 +51,15 @@ def shard_heads(num_q_heads: int, num_kv_heads: int, world: int, rank: int) -> H
     return HeadShard(rank, world, q, kv, rank * q, rank * kv)
 
 
+def shard_qkv_weight(q_weight: torch.Tensor, k_weight: torch.Tensor, v_weight: torch.Tensor,
+                     shard: HeadShard, head_dim: int) -> torch.Tensor:  # fmt: skip
+    """This rank's rows of the Q/K/V projections, fused ``[(Hq/N + 2 Hkv/N) * D, hidden]``: the
+    Q rows of its query heads, then the K and the V rows of its KV heads."""
+    qs = slice(shard.q_start * head_dim, (shard.q_start + shard.num_q_heads) * head_dim)
+    ks = slice(shard.kv_start * head_dim, (shard.kv_start + shard.num_kv_heads) * head_dim)
+    return torch.cat([q_weight[qs], k_weight[ks], v_weight[ks]]).contiguous()
+
+
 def shard_pool(pool: torch.Tensor, shard: HeadShard) -> torch.Tensor:
     """This rank's slice ``[..., num_blocks, Hkv/N, bs, D]`` of a full pool (contiguous copy)."""
     return pool[..., shard.kv_slice, :, :].contiguous()
