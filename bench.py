@@ -83,8 +83,8 @@ def parse() -> argparse.Namespace:
                     help="decode70b: layer pools kept resident (0 = as many as fit); layers "
                          "cycle through them, each still read in full from HBM")  # fmt: skip
     ap.add_argument("--shard-of", type=int, default=1,
-                    help="decode70b on 1 GPU: run rank 0's share of an N-way KV-head split "
-                         "(no collective), to measure the per-rank kernel alone")  # fmt: skip
+                    help="decode / decode70b on 1 GPU: run rank 0's share of an N-way KV-head "
+                         "split (no collective), to measure the per-rank kernel alone")  # fmt: skip
     args = ap.parse_args()
     if args.steps is None:
         args.steps = 200 if args.workload == "decode" and args.impl == "cuda" else 20
@@ -512,7 +512,8 @@ def run_cuda(args: argparse.Namespace, world: int, rank: int, local: int) -> dic
     # Every rank runs the same seeded batch (the block tables and slots are replicated, as the
     # scheduler's decisions are); rank r holds KV heads [r*8/N, (r+1)*8/N) and their query heads.
     case = decode_workload(seed=0, batch=args.batch, num_blocks=args.pool_blocks)
-    sh = shard_heads(case.num_q_heads, case.num_kv_heads, world, rank)
+    split = world if world > 1 else max(1, args.shard_of)
+    sh = shard_heads(case.num_q_heads, case.num_kv_heads, split, rank)
     B, hq, hkv, d, bs = case.batch, sh.num_q_heads, sh.num_kv_heads, case.head_dim, 16
     dt = torch.bfloat16
     g = torch.Generator(device=dev).manual_seed(1000 + rank)
@@ -531,8 +532,9 @@ def run_cuda(args: argparse.Namespace, world: int, rank: int, local: int) -> dic
     ws = torch.empty(ops.decode_workspace_size(B, hq, hkv, d, bt.shape[1], bs, dt),
                      dtype=torch.uint8, device=dev)  # fmt: skip
     scale = d**-0.5
-    kv_bytes = case.kv_bytes(2)  # all 8 KV heads: what the whole job reads per step
-    kv_bytes_rank = kv_bytes * hkv // case.num_kv_heads
+    kv_bytes_rank = case.kv_bytes(2) * hkv // case.num_kv_heads
+    # What the whole job reads per step: all 8 KV heads (only this rank's with --shard-of).
+    kv_bytes = case.kv_bytes(2) if world > 1 else kv_bytes_rank
     # Algorithmic bytes of one decode launch on this rank: its KV read + q in + out rows +
     # block-table entries and context lengths.
     blocks_read = int(((case.context_lens.astype(np.int64) + bs - 1) // bs).sum())
@@ -767,7 +769,9 @@ def run_cuda(args: argparse.Namespace, world: int, rank: int, local: int) -> dic
             "vs_baseline": None,
             "dtype": "bf16",
             "data": "synthetic",
-            "config": config(args, world),
+            "config": config(args, world) if split == world else {
+                **config(args, 1), "parallelism": f"one GPU running rank 0's share of a "
+                f"{split}-way KV-head split ({hkv} KV / {hq} query heads), no collective"},
             "frac_of_hbm_peak": round(value / world / peak, 4),
             "roofline": {
                 "bound": "hbm",
