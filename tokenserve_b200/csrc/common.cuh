@@ -63,6 +63,18 @@ __device__ __forceinline__ void fence_mbar_init() {
   asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
 }
 
+// Programmatic dependent launch (sm_90+): a kernel launched with the programmatic-serialization
+// attribute may start while the previous kernel on its stream still runs, once that kernel has
+// called launch_dependents (or exited); it must call wait_prior_grid() before it touches memory
+// the previous kernel may write or the caller wrote before it. Both are no-ops for a kernel
+// launched without the attribute.
+__device__ __forceinline__ void allow_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void wait_prior_grid() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }

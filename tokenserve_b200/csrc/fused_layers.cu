@@ -145,6 +145,7 @@ __global__ void rope_and_cache_kernel(const T* __restrict__ qkv, int64_t qkv_str
                                       const float* __restrict__ inv_freq, int hq, int hkv, int d,
                                       int block_size, int64_t num_slots,
                                       int32_t* __restrict__ error_flag) {
+  ts::allow_dependents();  // the attention kernels after it wait for this grid on the device
   const int64_t t = blockIdx.x;
   const T* row = qkv + t * qkv_stride;
   const float pos = float(__ldg(positions + t));
@@ -201,6 +202,7 @@ __global__ void rope_and_cache_vec_kernel(const T* __restrict__ qkv, int64_t qkv
                                           const float* __restrict__ inv_freq, int hq, int hkv,
                                           int d, int block_size, int64_t num_slots,
                                           int32_t* __restrict__ error_flag) {
+  ts::allow_dependents();  // the attention kernels after it wait for this grid on the device
   constexpr int E = Vec<T>::E;
   const int64_t t = blockIdx.x;
   const T* row = qkv + t * qkv_stride;

@@ -349,6 +349,10 @@ __device__ void prep_dynamic(DecodeArgs& a, int* warp_sums, int cnt, int b0) {
 // word and arrival counters, and writes the output rows of empty contexts.
 template <typename T>
 __global__ void __launch_bounds__(kPrepThreads) decode_prep_kernel(DecodeArgs a, int row_elems) {
+  // The decode grid may launch now (it waits for this grid before reading anything); this grid
+  // itself waits for the work before it on the stream (e.g. the K/V append) to be complete.
+  ts::allow_dependents();
+  ts::wait_prior_grid();
   __shared__ int warp_sums[32];
   const int B = a.batch, H = a.num_kv_heads;
   const int per = (B + blockDim.x - 1) / blockDim.x;
@@ -452,6 +456,10 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int g = lane >> 2, t = lane & 3;
+  // Launched programmatically after the prep kernel (or after the caller's previous kernel when
+  // the plan is reused): everything below reads the plan, the tables, the query or the pool, so
+  // wait until the grid before this one has completed and its writes are visible.
+  ts::wait_prior_grid();
   if (a.reuse_plan) {
     // The plan must have been made for this batch, head count, table width and grid.
     if (__ldg(a.header + 6) != a.batch || __ldg(a.header + 7) != a.num_kv_heads ||
@@ -996,8 +1004,30 @@ int launch_fast(DecodeArgs a, const CUtensorMap& km, const CUtensorMap& vm, cuda
     if (dev >= 0 && dev < 64) attr_done[dev] = true;
   }
   a.reuse_plan = plan ? 0 : 1;
-  if (plan) decode_prep_kernel<T><<<1, kPrepThreads, 0, s>>>(a, a.num_q_heads * D);
-  kern<<<num_sms(), kWarps * 32, G::kSmemBytes, s>>>(km, vm, a);
+  // Both kernels are launched with programmatic stream serialization: each may be scheduled
+  // while the kernel before it still runs and waits on the device (griddepcontrol.wait) before
+  // reading its inputs, so the decode grid's launch overlaps the prep kernel.
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.stream = s;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (plan) {
+    cfg.gridDim = dim3(1);
+    cfg.blockDim = dim3(kPrepThreads);
+    cfg.dynamicSmemBytes = 0;
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, decode_prep_kernel<T>, a, a.num_q_heads * D);
+    if (e != cudaSuccess) return ts::set_error(static_cast<int>(e), "paged_decode: prep launch: %s",
+                                               cudaGetErrorString(e));
+  }
+  cfg.gridDim = dim3(num_sms());
+  cfg.blockDim = dim3(kWarps * 32);
+  cfg.dynamicSmemBytes = G::kSmemBytes;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, km, vm, a);
+  if (e != cudaSuccess)
+    return ts::set_error(static_cast<int>(e), "paged_decode: launch: %s", cudaGetErrorString(e));
   return ts::launch_status("paged_decode");
 }
 

@@ -38,6 +38,9 @@ __global__ void __launch_bounds__(256) reshape_and_cache_kernel(
     const int64_t* __restrict__ slot_mapping, int64_t num_tokens, int heads, int row_bytes,
     int block_size, int64_t num_slots, const int32_t* __restrict__ tags,
     int32_t* __restrict__ tag_pool, int32_t* __restrict__ error_flag) {
+  // A decode's prep kernel launched programmatically after this one may start now: it waits
+  // for this grid on the device before it reads anything.
+  ts::allow_dependents();
   using V = typename VecType<VEC>::T;
   const int vec_per_row = row_bytes / VEC;
   const int vec_per_tok = heads * vec_per_row;
