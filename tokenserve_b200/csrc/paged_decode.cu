@@ -44,7 +44,7 @@ namespace {
 #define TS_DECODE_PART_BLOCKS 64  // largest work item, in blocks
 #endif
 #ifndef TS_DECODE_STATIC_MAX_BLOCKS
-#define TS_DECODE_STATIC_MAX_BLOCKS 80  // static split below this many blocks per warp
+#define TS_DECODE_STATIC_MAX_BLOCKS 64  // static split while a group's range is at most this
 #endif
 #ifndef TS_DECODE_STAGES_D128
 #define TS_DECODE_STAGES_D128 3  // ring stages per warp at head_dim 128
@@ -231,11 +231,14 @@ __device__ void prep_static(DecodeArgs& a, int* warp_sums, long long WB, int run
   const int B = a.batch;
   const int NG = int(min((long long)(a.grid_warps / a.num_kv_heads), WB));
   const GroupSplit gsp(int(WB), NG > 0 ? NG : 1);
+  // A group spans at most kPartBlocks blocks (the prep kernel's choice of split), so each
+  // group a sequence overlaps holds exactly one of its partitions: the count is the number of
+  // groups its blocks [u, u + n) touch.
   int c = 0;
   int u = run0;
   for (int i = 0; i < cnt; ++i) {
     const int n = blocks_of(ctx_of(a, b0 + i));
-    if (n > 0) for_each_chunk(u, u + n, gsp, [&](int, int, int, int) { ++c; });
+    if (n > 0) c += gsp.group_of(u + n - 1) - gsp.group_of(u) + 1;
     u += n;
   }
   int total = 0;
@@ -278,7 +281,6 @@ constexpr int kClassFull = kPartsCap + 1;
 constexpr int kSortBuckets = kClassFull + 1 + kPartBlocks;
 
 __device__ void prep_dynamic(DecodeArgs& a, int* warp_sums, int cnt, int b0) {
-  static_assert(kSortBuckets <= kPrepThreads, "one sort bucket per prep thread");
   __shared__ int bucket[kSortBuckets];  // counts, then cursors
   const int B = a.batch, H = a.num_kv_heads;
   for (int i = threadIdx.x; i < kSortBuckets; i += blockDim.x) bucket[i] = 0;
@@ -311,10 +313,20 @@ __device__ void prep_dynamic(DecodeArgs& a, int* warp_sums, int cnt, int b0) {
     }
   }
   __syncthreads();
+  // Counts -> cursors (exclusive prefix in bucket order); thread i owns a contiguous run of
+  // buckets, so any block size covers them.
   int sorted = 0;
-  const int first = block_exclusive_scan(
-      threadIdx.x < kSortBuckets ? bucket[threadIdx.x] : 0, &sorted, warp_sums);
-  if (threadIdx.x < kSortBuckets) bucket[threadIdx.x] = first;  // every count was read above
+  const int per_b = (kSortBuckets + blockDim.x - 1) / blockDim.x;
+  const int bk0 = min(kSortBuckets, int(threadIdx.x) * per_b);
+  const int bk1 = min(kSortBuckets, bk0 + per_b);
+  int run_sum = 0;
+  for (int k = bk0; k < bk1; ++k) run_sum += bucket[k];
+  int first = block_exclusive_scan(run_sum, &sorted, warp_sums);  // every count was read above
+  for (int k = bk0; k < bk1; ++k) {
+    const int c = bucket[k];
+    bucket[k] = first;
+    first += c;
+  }
   __syncthreads();
   // Partition p of sequence b -> claim position q (items q * H + h, one per head).
   auto put = [&](int q, int b, int p, int n, int c0, int ctx) {
@@ -343,7 +355,7 @@ __device__ void prep_dynamic(DecodeArgs& a, int* warp_sums, int cnt, int b0) {
   }
 }
 
-// One CTA of kPrepThreads threads: chooses the split (static below kStaticMaxBlocksPerWarp blocks per
+// One CTA (up to kPrepThreads threads, as many as the batch needs): chooses the split (static below kStaticMaxBlocksPerWarp blocks per
 // warp, dynamic above), writes the partition descriptors and the per-sequence partition
 // prefixes that place each (sequence, head)'s partial results, zeroes the claim counter, status
 // word and arrival counters, and writes the output rows of empty contexts.
@@ -378,7 +390,10 @@ __global__ void __launch_bounds__(kPrepThreads) decode_prep_kernel(DecodeArgs a,
   if (threadIdx.x % 32 == 0 && wsum) atomicAdd(&total_smem, wsum);
   __syncthreads();
   const long long WB = total_smem;
-  if (WB * H >= (long long)kStaticMaxBlocksPerWarp * a.grid_warps) {
+  // Static split while every group of the split spans at most min(kStaticMaxBlocksPerWarp,
+  // kPartBlocks) blocks (ceil(WB / NG)); dynamic claiming above.
+  const long long NG = min((long long)(a.grid_warps / H), WB);
+  if (NG <= 0 || (WB + NG - 1) / NG > (long long)min(kStaticMaxBlocksPerWarp, kPartBlocks)) {
     prep_dynamic(a, warp_sums, cnt, b0);
   } else {
     int total_blocks = 0;
@@ -1015,8 +1030,10 @@ int launch_fast(DecodeArgs a, const CUtensorMap& km, const CUtensorMap& vm, cuda
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   if (plan) {
+    // One thread per sequence up to kPrepThreads (fewer threads: cheaper block-wide barriers
+    // and scans, the prep kernel's critical path at small batches).
     cfg.gridDim = dim3(1);
-    cfg.blockDim = dim3(kPrepThreads);
+    cfg.blockDim = dim3(std::min(kPrepThreads, std::max(64, (a.batch + 31) / 32 * 32)));
     cfg.dynamicSmemBytes = 0;
     const cudaError_t e = cudaLaunchKernelEx(&cfg, decode_prep_kernel<T>, a, a.num_q_heads * D);
     if (e != cudaSuccess) return ts::set_error(static_cast<int>(e), "paged_decode: prep launch: %s",
