@@ -674,6 +674,24 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
     }
   };
 
+  // Output destinations, one per lane (n_out <= 64): lane o holds destination o and lane o
+  // destination o + 32, so a finished item finds each base with a shuffle instead of a
+  // dependent global load per destination.
+  unsigned long long dst_lo = 0, dst_hi = 0;
+  if (a.n_out > 0) {
+    if (lane < a.n_out) dst_lo = reinterpret_cast<unsigned long long>(a.outs[lane]);
+    if (lane + 32 < a.n_out) dst_hi = reinterpret_cast<unsigned long long>(a.outs[lane + 32]);
+  } else {
+    dst_lo = reinterpret_cast<unsigned long long>(a.out);
+  }
+  const int n_dst = a.n_out > 0 ? a.n_out : 1;
+  // Row (sequence b, query head j) of destination o, and whether its rows take 16-byte stores.
+  auto dst_row = [&](int o, int b, int j, bool& vec) -> T* {
+    const unsigned long long base = __shfl_sync(0xffffffffu, o < 32 ? dst_lo : dst_hi, o & 31);
+    vec = ((base | (unsigned long long)(a.out_row_stride * sizeof(T))) & 15) == 0;
+    return reinterpret_cast<T*>(base) + int64_t(b) * a.out_row_stride + int64_t(a.out_head0 + j) * D;
+  };
+
   auto finish_item = [&]() {
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt)
@@ -686,23 +704,47 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
         l_run[nt][j] = l;
       }
     if (it.nparts == 1) {
-      const int n_dst = a.n_out > 0 ? a.n_out : 1;
+      // After the transpose lane (g, t) holds, for head nt * 8 + g, the words of dims
+      // 16 mt + 2t (lo) and 16 mt + 8 + 2t (hi): a quad covers 16-byte chunk c = 2 mt (+1 for
+      // hi). Each chunk is gathered into lane t = c % 4 of its quad and stored as one vector.
+      constexpr int NCH = 2 * MTILES;  // 16-byte chunks per head row
+      uint32_t pw[NT][MTILES][2];
+      uint4 ch[NT][NCH / 4];
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+        const float i0 = l_run[nt][0] > 0.f ? 1.f / l_run[nt][0] : 0.f;
+        const float i1 = l_run[nt][1] > 0.f ? 1.f / l_run[nt][1] : 0.f;
+#pragma unroll
+        for (int mt = 0; mt < MTILES; ++mt) {
+          pw[nt][mt][0] = movmatrix_pack<Mma>(oacc[nt][mt][0] * i0, oacc[nt][mt][1] * i1);
+          pw[nt][mt][1] = movmatrix_pack<Mma>(oacc[nt][mt][2] * i0, oacc[nt][mt][3] * i1);
+        }
+#pragma unroll
+        for (int c = 0; c < NCH; ++c) {
+          uint32_t v[4];
+#pragma unroll
+          for (int w = 0; w < 4; ++w) v[w] = __shfl_sync(0xffffffffu, pw[nt][c / 2][c % 2], (g << 2) | w);
+          if (t == c % 4) ch[nt][c / 4] = make_uint4(v[0], v[1], v[2], v[3]);
+        }
+      }
 #pragma unroll 1
       for (int o = 0; o < n_dst; ++o) {
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) {
-          const float i0 = l_run[nt][0] > 0.f ? 1.f / l_run[nt][0] : 0.f;
-          const float i1 = l_run[nt][1] > 0.f ? 1.f / l_run[nt][1] : 0.f;
           const int head = nt * 8 + g;  // after the transpose a lane owns one head
-          uint32_t* orow =
-              reinterpret_cast<uint32_t*>(out_row<T, D>(a, o, it.b, it.h * a.group + head));
+          bool vec;
+          T* orow = dst_row(o, it.b, it.h * a.group + head, vec);
+          if (head >= a.group) continue;
+          if (vec) {
 #pragma unroll
-          for (int mt = 0; mt < MTILES; ++mt) {
-            const uint32_t lo = movmatrix_pack<Mma>(oacc[nt][mt][0] * i0, oacc[nt][mt][1] * i1);
-            const uint32_t hi = movmatrix_pack<Mma>(oacc[nt][mt][2] * i0, oacc[nt][mt][3] * i1);
-            if (head < a.group) {
-              orow[(mt * 16 + 2 * t) / 2] = lo;
-              orow[(mt * 16 + 8 + 2 * t) / 2] = hi;
+            for (int j = 0; j < NCH / 4; ++j)
+              *reinterpret_cast<uint4*>(orow + 8 * (4 * j + t)) = ch[nt][j];
+          } else {
+            uint32_t* w32 = reinterpret_cast<uint32_t*>(orow);
+#pragma unroll
+            for (int mt = 0; mt < MTILES; ++mt) {
+              w32[(mt * 16 + 2 * t) / 2] = pw[nt][mt][0];
+              w32[(mt * 16 + 8 + 2 * t) / 2] = pw[nt][mt][1];
             }
           }
         }
@@ -795,11 +837,34 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
       for (int i = 0; i < PER; ++i) acc[i] += w * __ldcg(src + lane + 32 * i);
     }
     const float inv = lsum > 0.f ? 1.f / lsum : 0.f;
-    if (hd < a.group) {
-      const int n_dst = a.n_out > 0 ? a.n_out : 1;
+    // Lane (hd, kq = lane / NT8) holds dims kq + LPH * i of head hd. Gather each 16-byte chunk
+    // (8 consecutive dims) of a head into lane kq = chunk % LPH and store it as one vector.
+    constexpr int LPH = 32 / NT8;     // lanes per head
+    constexpr int NCH = D / 8;        // 16-byte chunks per head row
+    const int kq = lane / NT8;
+    uint4 mch[NCH / LPH];
+#pragma unroll
+    for (int c = 0; c < NCH; ++c) {
+      float f[8];
+#pragma unroll
+      for (int m = 0; m < 8; ++m) {
+        const int dim = 8 * c + m;
+        f[m] = __shfl_sync(0xffffffffu, acc[dim / LPH], hd + NT8 * (dim % LPH)) * inv;
+      }
+      if (kq == c % LPH)
+        mch[c / LPH] = make_uint4(Mma::pack(f[0], f[1]), Mma::pack(f[2], f[3]), Mma::pack(f[4], f[5]),
+                                  Mma::pack(f[6], f[7]));
+    }
 #pragma unroll 1
-      for (int o = 0; o < n_dst; ++o) {
-        T* orow = out_row<T, D>(a, o, it.b, it.h * a.group + hd);
+    for (int o = 0; o < n_dst; ++o) {
+      bool vec;
+      T* orow = dst_row(o, it.b, it.h * a.group + hd, vec);  // every lane takes the shuffle
+      if (hd >= a.group) continue;
+      if (vec) {
+#pragma unroll
+        for (int j = 0; j < NCH / LPH; ++j)
+          *reinterpret_cast<uint4*>(orow + 8 * (j * LPH + kq)) = mch[j];
+      } else {
 #pragma unroll
         for (int i = 0; i < PER; ++i) orow[(lane + 32 * i) / NT8] = ts::from_float<T>(acc[i] * inv);
       }
