@@ -75,10 +75,13 @@ def parse() -> argparse.Namespace:
     ap.add_argument("--skip-e2e", action="store_true", help="profiling runs only")
     ap.add_argument("--skip-parity", action="store_true",
                     help="profiling runs only: no oracle check of the timed output")  # fmt: skip
-    ap.add_argument("--collective", choices=["auto", "fused", "nccl"], default="auto",
-                    help="decode and decode70b at N>1: decode writing every rank's output "
-                         "buffer over NVLink (fused) or decode + NCCL all-gather on a second "
-                         "stream; auto: fused below 8 ranks, NCCL at 8")  # fmt: skip
+    ap.add_argument("--collective", choices=["auto", "fused", "pull", "nccl"], default="auto",
+                    help="exchange of the attention outputs at N>1: fused (the decode stores "
+                         "its rows into every rank's buffer over NVLink), pull (the decode writes "
+                         "its own buffer and publishes; a gather kernel then reads the other "
+                         "ranks' rows over NVLink), nccl (all-gather on a second stream); auto: "
+                         "pull for the decode op, fused below 8 ranks and NCCL at 8 for "
+                         "decode70b")  # fmt: skip
     ap.add_argument("--resident-layers", type=int, default=0,
                     help="decode70b: layer pools kept resident (0 = as many as fit); layers "
                          "cycle through them, each still read in full from HBM")  # fmt: skip
@@ -148,7 +151,7 @@ def collective_for(args: argparse.Namespace, world: int) -> str:
         return "none"
     if args.collective != "auto":
         return args.collective
-    return "nccl" if world >= 8 else "fused"
+    return "pull"
 
 
 # ----------------------------------------------------------------------------- CPU side
@@ -547,11 +550,12 @@ def run_cuda(args: argparse.Namespace, world: int, rank: int, local: int) -> dic
     # overlap step i+1).
     nbuf = 2
     pg = None
-    if collective == "fused":
+    if collective in ("fused", "pull"):
         from tokenserve_b200.peer import PeerGather
 
         pg = PeerGather(B, hq, d, dt, nbuf=nbuf)
         full = pg.full
+    pull = collective == "pull"
     else:
         full = [torch.empty(B, hq * world, d, dtype=dt, device=dev) for _ in range(nbuf)]
     outs = [torch.empty(B, hq, d, dtype=dt, device=dev) for _ in range(nbuf)]
@@ -569,10 +573,13 @@ def run_cuda(args: argparse.Namespace, world: int, rank: int, local: int) -> dic
                 out_ev.record(stream)
             return outs[p]
         if pg is not None:
-            epoch = pg.decode(p, qq, kpool, vpool, bt, cl, scale, ws)
+            epoch = pg.decode(p, qq, kpool, vpool, bt, cl, scale, ws, pull=pull)
             if out_ev is not None:
                 out_ev.record(stream)
-            pg.wait(epoch)
+            if pull:
+                pg.gather(p, epoch)
+            else:
+                pg.wait(epoch)
             if ex_ev is not None:
                 ex_ev.record(stream)
             return full[p]
@@ -755,7 +762,7 @@ def run_cuda(args: argparse.Namespace, world: int, rank: int, local: int) -> dic
         peak, peak_kind = peaks()
         achieved = decode_bytes / dec_avg / 1e9
         value = kv_bytes * args.steps / elapsed / 1e9
-        launches = 3 if world == 1 else (4 if pg is not None else 3)
+        launches = 3 if world == 1 else (4 if pg is not None else 3)  # + wait or gather kernel
         line = {
             "metric": METRIC,
             "value": round(value, 2),
@@ -804,7 +811,10 @@ def run_cuda(args: argparse.Namespace, world: int, rank: int, local: int) -> dic
         if world > 1:
             line["exchange"] = {
                 "collective": collective,
-                "how": ("fused: K2 stores each finished output row into every rank's [B, 32, D] "
+                "how": ("pull: K2 writes this rank's rows into its own [B, 32, D] buffer and "
+                        "publishes its epoch to every rank; a gather kernel waits (bounded) for "
+                        "all epochs and reads the other ranks' rows over NVLink" if pull else
+                        "fused: K2 stores each finished output row into every rank's [B, 32, D] "
                         "buffer over NVLink, then a bounded device wait for all ranks' epoch"
                         if pg is not None else
                         "NCCL all_gather of [B, Hq/N, D] on a second stream, overlapping the "
@@ -894,6 +904,8 @@ def run_decode70b(args: argparse.Namespace, world: int, rank: int, local: int) -
     freed = [torch.cuda.Event() for _ in range(nbuf)]
     kv_bytes_rank = case.kv_bytes(2) * hkv_r // case.num_kv_heads
     collective = args.collective if args.collective != "auto" else ("nccl" if world >= 8 else "fused")
+    if collective == "pull":
+        collective = "fused"  # decode70b runs the push form of the peer exchange
     fused = world > 1 and collective == "fused"
     pg = None
     if fused:

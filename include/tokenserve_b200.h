@@ -274,6 +274,39 @@ int ts_paged_decode_peer(void* const* dst_outs, int32_t world, int32_t rank,
                          size_t workspace_bytes, int32_t reuse_plan, void* stream);
 
 /*
+ * The pull form of the same exchange: this rank's rows go into its own buffer only
+ * (dst_outs[rank], at head offset rank * num_q_heads, fast local stores), and the grid's last
+ * CTA publishes `epoch` into signals[r][rank] for every r as above; each rank then fetches the
+ * others' rows with ts_gather_peers. Arguments as ts_paged_decode_peer.
+ *
+ * Replaces: the same eager attention per KV-head shard; the exchange has no counterpart in the
+ * reference, which runs on one CPU process.
+ */
+int ts_paged_decode_publish(void* const* dst_outs, int32_t world, int32_t rank,
+                            int32_t* const* signals, uint32_t epoch, const void* query,
+                            int64_t query_token_stride, const void* key_pool,
+                            const void* value_pool, const int32_t* block_tables,
+                            int32_t max_blocks_per_seq, const int32_t* context_lens,
+                            int32_t batch, int32_t num_q_heads, int32_t num_kv_heads,
+                            int32_t head_dim, int32_t block_size, int64_t num_blocks,
+                            float scale, int32_t dtype, void* workspace, size_t workspace_bytes,
+                            int32_t reuse_plan, void* stream);
+
+/*
+ * Completes a pull exchange on this rank: waits on the device (bounded, about a second) until
+ * local_signals[r] >= epoch for every r < world, then copies every other rank's
+ * [batch][heads_per_rank][head_dim] slice from that rank's buffer fulls[r] (read over NVLink)
+ * into the same rows and head offset of fulls[rank]. fulls is a device array of world pointers
+ * (each rank's [batch][world * heads_per_rank][head_dim] buffer as mapped here). On a timeout
+ * nothing is copied by the CTAs that gave up and *status (device int32) is set to 3.
+ * heads_per_rank * head_dim * element size must be a multiple of 16 bytes.
+ */
+int ts_gather_peers(void* const* fulls, int32_t world, int32_t rank,
+                    const int32_t* local_signals, uint32_t epoch, int32_t batch,
+                    int32_t heads_per_rank, int32_t head_dim, int32_t dtype, int32_t* status,
+                    void* stream);
+
+/*
  * Waits on the device until local_signals[r] >= epoch for every r < world (every rank's
  * ts_paged_decode_peer of that epoch has finished writing into this rank's buffer). The wait
  * is bounded (about a second); on timeout *status (device int32) is set to 3 and the kernel

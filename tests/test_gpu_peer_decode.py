@@ -21,7 +21,7 @@ import torch
 
 from oracle import attention as oatt
 from tokenserve_b200 import ops
-from tokenserve_b200.sharding import shard_heads, shard_pool
+from tokenserve_b200.sharding import gather_heads, heads_from_gathered, shard_heads, shard_pool
 from tokenserve_b200.workloads import small_paged_case
 
 pytestmark = pytest.mark.gpu
@@ -184,15 +184,24 @@ def _rank(rank: int, world: int, port: int, q) -> None:  # type: ignore[no-untyp
                                                    bt.shape[1], 16, torch.bfloat16),
                          dtype=torch.uint8, device=dev)  # fmt: skip
         pg = PeerGather(case.batch, sh.num_q_heads, d, torch.bfloat16, nbuf=2)
-        for step in range(3):
-            e = pg.decode(step % 2, qr, kr, vr, bt, cl, d**-0.5, ws)
-            pg.wait(e)
-        torch.cuda.synchronize()
-        pg.check()
         ref = oatt.paged_decode_np(qf.float().numpy(), kp.float().numpy(), vp.float().numpy(),
                                    case.block_tables, case.context_lens, d**-0.5)  # fmt: skip
-        got = pg.full[0].float().cpu().numpy()
-        q.put((rank, float(np.abs(got - ref).max()), float(np.abs(ref).max())))
+        # This rank's own decode, brought together with the peer's by NCCL: the exchanged
+        # buffer must equal it bit for bit, in both forms of the exchange.
+        own = torch.empty(case.batch, sh.num_q_heads, d, dtype=torch.bfloat16, device=dev)
+        ops.paged_decode(own, qr, kr, vr, bt, cl, d**-0.5, ws)
+        want = heads_from_gathered(gather_heads(own))
+        errs = []
+        for pull in (False, True):  # push: rows stored into every rank; pull: gathered after
+            for step in range(3):
+                e = pg.decode(step % 2, qr, kr, vr, bt, cl, d**-0.5, ws, pull=pull)
+                pg.gather(step % 2, e) if pull else pg.wait(e)
+            torch.cuda.synchronize()
+            pg.check()
+            assert torch.equal(pg.full[0], want), f"exchange (pull={pull}) differs from own decode"
+            errs.append(float(np.abs(pg.full[0].float().cpu().numpy() - ref).max()))
+            dist.barrier()
+        q.put((rank, max(errs), float(np.abs(ref).max())))
         pg.close()
     finally:
         dist.destroy_process_group()

@@ -95,8 +95,9 @@ struct DecodeArgs {
   int n_out;
   int64_t out_row_stride;  // elements
   int out_head0;
-  // Completion signal (n_out > 0): the grid's last CTA stores `epoch` into
-  // signals[r][signal_index] for every r < n_out, after every CTA's output stores.
+  // Completion signal (n_signals > 0): the grid's last CTA stores `epoch` into
+  // signals[r][signal_index] for every r < n_signals, after every CTA's output stores.
+  int n_signals;
   int* const* signals;
   int signal_index;
   unsigned epoch;
@@ -982,14 +983,14 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
   // system-wide before its CTA counts itself done; the last CTA then publishes the epoch to
   // every rank. The last CTA also re-zeroes the claim counter and this counter: every CTA has
   // stopped claiming, and the next launch on the stream may reuse the plan.
-  if (a.n_out > 0) __threadfence_system();
+  if (a.n_signals > 0) __threadfence_system();
   __syncthreads();
   if (threadIdx.x == 0) {
     const int done = atomicAdd(a.header + 4, 1);
     if (done == int(gridDim.x) - 1) {
-      if (a.n_out > 0) {
+      if (a.n_signals > 0) {
         __threadfence_system();
-        for (int r = 0; r < a.n_out; ++r) {
+        for (int r = 0; r < a.n_signals; ++r) {
           int* flag = a.signals[r] + a.signal_index;
           asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(flag), "r"(a.epoch) : "memory");
         }
@@ -1204,6 +1205,7 @@ int paged_decode_call(void* out, const void* query, int64_t query_token_stride,
   a.n_out = 0;
   a.out_row_stride = int64_t(num_q_heads) * head_dim;
   a.out_head0 = 0;
+  a.n_signals = 0;
   a.signals = nullptr;
   a.signal_index = 0;
   a.epoch = 0;
@@ -1372,6 +1374,7 @@ extern "C" int ts_paged_decode_no_alloc(void* out, const void* query, int64_t qu
   a.n_out = 0;
   a.out_row_stride = int64_t(num_q_heads) * head_dim;
   a.out_head0 = 0;
+  a.n_signals = 0;
   a.signals = nullptr;
   a.signal_index = 0;
   a.epoch = 0;
@@ -1430,15 +1433,17 @@ bool on_current_device(const void* p) {
 
 }  // namespace
 
-extern "C" int ts_paged_decode_peer(void* const* dst_outs, int32_t world, int32_t rank,
-                                    int32_t* const* signals, uint32_t epoch, const void* query,
-                                    int64_t query_token_stride, const void* key_pool,
-                                    const void* value_pool, const int32_t* block_tables,
-                                    int32_t max_blocks_per_seq, const int32_t* context_lens,
-                                    int32_t batch, int32_t num_q_heads, int32_t num_kv_heads,
-                                    int32_t head_dim, int32_t block_size, int64_t num_blocks,
-                                    float scale, int32_t dtype, void* workspace,
-                                    size_t workspace_bytes, int32_t reuse_plan, void* stream) {
+namespace {
+
+int paged_decode_exchange(bool pull, void* const* dst_outs, int32_t world, int32_t rank,
+                          int32_t* const* signals, uint32_t epoch, const void* query,
+                          int64_t query_token_stride, const void* key_pool,
+                          const void* value_pool, const int32_t* block_tables,
+                          int32_t max_blocks_per_seq, const int32_t* context_lens, int32_t batch,
+                          int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim,
+                          int32_t block_size, int64_t num_blocks, float scale, int32_t dtype,
+                          void* workspace, size_t workspace_bytes, int32_t reuse_plan,
+                          void* stream) {
   if (world < 1 || world > 64 || rank < 0 || rank >= world || epoch == 0)
     return ts::set_error(TS_ERR_INVALID_ARGUMENT,
                          "paged_decode_peer: bad world %d / rank %d / epoch %u", world, rank, epoch);
@@ -1487,10 +1492,13 @@ extern "C" int ts_paged_decode_peer(void* const* dst_outs, int32_t world, int32_
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   DecodeArgs a;
   a.out = nullptr;
-  a.outs = dst_outs;
-  a.n_out = world;
+  // push: this rank's rows go into every rank's buffer; pull: into its own buffer only, and
+  // the other ranks fetch them (ts_gather_peers).
+  a.outs = pull ? dst_outs + rank : dst_outs;
+  a.n_out = pull ? 1 : world;
   a.out_row_stride = int64_t(world) * num_q_heads * head_dim;
   a.out_head0 = rank * num_q_heads;
+  a.n_signals = world;
   a.signals = reinterpret_cast<int* const*>(signals);
   a.signal_index = rank;
   a.epoch = epoch;
@@ -1526,6 +1534,107 @@ extern "C" int ts_paged_decode_peer(void* const* dst_outs, int32_t world, int32_
   }
   TS_FAST_PEER(__half)
 #undef TS_FAST_PEER
+}
+
+}  // namespace
+
+extern "C" int ts_paged_decode_peer(void* const* dst_outs, int32_t world, int32_t rank,
+                                    int32_t* const* signals, uint32_t epoch, const void* query,
+                                    int64_t query_token_stride, const void* key_pool,
+                                    const void* value_pool, const int32_t* block_tables,
+                                    int32_t max_blocks_per_seq, const int32_t* context_lens,
+                                    int32_t batch, int32_t num_q_heads, int32_t num_kv_heads,
+                                    int32_t head_dim, int32_t block_size, int64_t num_blocks,
+                                    float scale, int32_t dtype, void* workspace,
+                                    size_t workspace_bytes, int32_t reuse_plan, void* stream) {
+  return paged_decode_exchange(false, dst_outs, world, rank, signals, epoch, query,
+                               query_token_stride, key_pool, value_pool, block_tables,
+                               max_blocks_per_seq, context_lens, batch, num_q_heads, num_kv_heads,
+                               head_dim, block_size, num_blocks, scale, dtype, workspace,
+                               workspace_bytes, reuse_plan, stream);
+}
+
+extern "C" int ts_paged_decode_publish(void* const* dst_outs, int32_t world, int32_t rank,
+                                       int32_t* const* signals, uint32_t epoch,
+                                       const void* query, int64_t query_token_stride,
+                                       const void* key_pool, const void* value_pool,
+                                       const int32_t* block_tables, int32_t max_blocks_per_seq,
+                                       const int32_t* context_lens, int32_t batch,
+                                       int32_t num_q_heads, int32_t num_kv_heads,
+                                       int32_t head_dim, int32_t block_size, int64_t num_blocks,
+                                       float scale, int32_t dtype, void* workspace,
+                                       size_t workspace_bytes, int32_t reuse_plan, void* stream) {
+  return paged_decode_exchange(true, dst_outs, world, rank, signals, epoch, query,
+                               query_token_stride, key_pool, value_pool, block_tables,
+                               max_blocks_per_seq, context_lens, batch, num_q_heads, num_kv_heads,
+                               head_dim, block_size, num_blocks, scale, dtype, workspace,
+                               workspace_bytes, reuse_plan, stream);
+}
+
+// Waits (bounded) until every rank has published `epoch` into signals[0..world), then copies
+// every other rank's [batch][heads_per_rank][head_dim] slice out of that rank's full buffer (read
+// over NVLink) into the same place of this rank's buffer, 16 bytes a thread. On a timeout the
+// CTA copies nothing and sets *status = 3.
+__global__ void __launch_bounds__(256) gather_peers_kernel(uint8_t* const* fulls, int world,
+                                                           int rank, const int* signals,
+                                                           unsigned epoch, int batch,
+                                                           int64_t row_bytes, int64_t slice_bytes,
+                                                           int* status) {
+  __shared__ int ready;
+  if (threadIdx.x == 0) ready = 1;
+  __syncthreads();
+  if (threadIdx.x < world) {
+    bool ok = false;
+    for (long long i = 0; i < (1LL << 20) && !ok; ++i) {
+      unsigned v;
+      asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(signals + threadIdx.x)
+                   : "memory");
+      ok = int(v - epoch) >= 0;
+      if (!ok) __nanosleep(256);
+    }
+    if (!ok) {
+      ready = 0;
+      atomicExch(status, 3);
+    }
+  }
+  __syncthreads();
+  if (!ready) return;
+  uint8_t* mine = fulls[rank];
+  const int64_t chunks = slice_bytes / 16;        // per row of one rank
+  const int64_t per_rank = int64_t(batch) * chunks;
+  const int64_t total = int64_t(world - 1) * per_rank;
+  for (int64_t c = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; c < total;
+       c += int64_t(gridDim.x) * blockDim.x) {
+    const int rr = int(c / per_rank);
+    const int r = rr < rank ? rr : rr + 1;
+    const int64_t rem = c - int64_t(rr) * per_rank;
+    const int64_t b = rem / chunks, k = rem - b * chunks;
+    const int64_t off = b * row_bytes + int64_t(r) * slice_bytes + k * 16;
+    *reinterpret_cast<uint4*>(mine + off) = *reinterpret_cast<const uint4*>(fulls[r] + off);
+  }
+}
+
+extern "C" int ts_gather_peers(void* const* fulls, int32_t world, int32_t rank,
+                               const int32_t* local_signals, uint32_t epoch, int32_t batch,
+                               int32_t heads_per_rank, int32_t head_dim, int32_t dtype,
+                               int32_t* status, void* stream) {
+  const int es = ts::dtype_size(dtype);
+  if (world < 1 || world > 64 || rank < 0 || rank >= world || epoch == 0 || batch < 0 ||
+      heads_per_rank <= 0 || head_dim <= 0 || es == 0 || !fulls || !local_signals || !status)
+    return ts::set_error(TS_ERR_INVALID_ARGUMENT, "gather_peers: bad arguments");
+  const int64_t slice_bytes = int64_t(heads_per_rank) * head_dim * es;
+  if (slice_bytes % 16)
+    return ts::set_error(TS_ERR_UNSUPPORTED, "gather_peers: a rank's row slice is not 16-byte sized");
+  if (!on_current_device(fulls) || !on_current_device(local_signals))
+    return ts::set_error(TS_ERR_INVALID_ARGUMENT,
+                         "gather_peers: fulls and signals must be in the current device's memory");
+  const int64_t chunks = int64_t(world - 1) * batch * (slice_bytes / 16);
+  const int grid = int(std::max<int64_t>(1, std::min<int64_t>(2 * num_sms(), (chunks + 255) / 256)));
+  gather_peers_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      reinterpret_cast<uint8_t* const*>(fulls), world, rank,
+      reinterpret_cast<const int*>(local_signals), epoch, batch, slice_bytes * world, slice_bytes,
+      reinterpret_cast<int*>(status));
+  return ts::launch_status("gather_peers");
 }
 
 extern "C" int ts_wait_peers(const int32_t* local_signals, int32_t world, uint32_t epoch,

@@ -59,6 +59,14 @@ _SIGNATURES: dict[str, tuple[object, list[object]]] = {
         [_p, _i32, _i32, _p, ctypes.c_uint32, _p, _i64, _p, _p, _p, _i32, _p, _i32, _i32, _i32,
          _i32, _i32, _i64, _f32, _i32, _p, ctypes.c_size_t, _i32, _p],
     ),
+    "ts_paged_decode_publish": (
+        ctypes.c_int,
+        [_p, _i32, _i32, _p, ctypes.c_uint32, _p, _i64, _p, _p, _p, _i32, _p, _i32, _i32, _i32,
+         _i32, _i32, _i64, _f32, _i32, _p, ctypes.c_size_t, _i32, _p],
+    ),
+    "ts_gather_peers": (
+        ctypes.c_int, [_p, _i32, _i32, _p, ctypes.c_uint32, _i32, _i32, _i32, _i32, _p, _p]
+    ),
     "ts_wait_peers": (ctypes.c_int, [_p, _i32, ctypes.c_uint32, _p, _p]),
     "ts_peer_alloc": (ctypes.c_int, [ctypes.c_size_t, ctypes.POINTER(ctypes.c_void_p)]),
     "ts_peer_free": (ctypes.c_int, [_p]),

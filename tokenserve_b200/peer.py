@@ -105,13 +105,17 @@ class PeerGather:
 
     def decode(self, p: int, query: torch.Tensor, key_pool: torch.Tensor, value_pool: torch.Tensor,
                block_tables: torch.Tensor, context_lens: torch.Tensor, scale: float,
-               workspace: torch.Tensor, reuse_plan: bool = False) -> int:  # fmt: skip
+               workspace: torch.Tensor, reuse_plan: bool = False, pull: bool = False) -> int:  # fmt: skip
+        """This rank's decode into buffer ``p``: its rows stored into every rank's buffer
+        (``pull=False``, then :meth:`wait`) or into its own only (``pull=True``, then
+        :meth:`gather`, which fetches the other ranks' rows). Returns the call's epoch."""
         nb, hkv, bs, d = ops._pool_dims(key_pool)
         hq = query.shape[1]
         qs = ops._rows(query, hq, d, "query")
         self.epoch += 1
         ws_bytes = workspace.numel() * workspace.element_size()
-        code = self.lib.ts_paged_decode_peer(
+        fn = self.lib.ts_paged_decode_publish if pull else self.lib.ts_paged_decode_peer
+        code = fn(
             ops._ptr(self.dst[p]), self.world, self.rank, ops._ptr(self.sig), self.epoch,
             ops._ptr(query), qs, ops._ptr(key_pool), ops._ptr(value_pool),
             ops._ptr(block_tables), block_tables.shape[1], ops._ptr(context_lens),
@@ -120,6 +124,16 @@ class PeerGather:
         )  # fmt: skip
         ops._check(code, "paged_decode_peer")
         return self.epoch
+
+    def gather(self, p: int, epoch: int) -> None:
+        """Enqueues, on the current stream, the wait for every rank's ``epoch`` and the copy of
+        their rows into this rank's buffer ``p`` (the pull form of the exchange)."""
+        b, h, d = self.shape
+        code = self.lib.ts_gather_peers(ops._ptr(self.dst[p]), self.world, self.rank,
+                                        ops._ptr(self.signals), epoch, b, h // self.world, d,
+                                        ops.DTYPE_CODES[self.dtype], ops._ptr(self.status),
+                                        ops._stream())  # fmt: skip
+        ops._check(code, "gather_peers")
 
     def wait(self, epoch: int) -> None:
         code = self.lib.ts_wait_peers(ops._ptr(self.signals), self.world, epoch,
