@@ -555,9 +555,9 @@ def run_cuda(args: argparse.Namespace, world: int, rank: int, local: int) -> dic
 
         pg = PeerGather(B, hq, d, dt, nbuf=nbuf)
         full = pg.full
-    pull = collective == "pull"
     else:
         full = [torch.empty(B, hq * world, d, dtype=dt, device=dev) for _ in range(nbuf)]
+    pull = collective == "pull"
     outs = [torch.empty(B, hq, d, dtype=dt, device=dev) for _ in range(nbuf)]
     gath = [torch.empty(world, B, hq, d, dtype=dt, device=dev) for _ in range(nbuf)]
     comm = torch.cuda.Stream(device=dev)

@@ -1,0 +1,48 @@
+"""bench.py's command line and JSON plumbing on the CPU (no kernels run).
+
+The bench only runs on a B200, so these checks keep its host-side parts honest between GPU runs:
+the file compiles, every workload name parses, and the reference arm (the oracle on the host
+cores) prints one JSON line with the contract's keys.
+"""
+
+from __future__ import annotations
+
+import json
+import py_compile
+import subprocess
+import sys
+
+from tests.conftest import ROOT
+
+
+def test_bench_compiles() -> None:
+    py_compile.compile(str(ROOT / "bench.py"), doraise=True)
+
+
+def test_bench_parses_every_workload() -> None:
+    sys.path.insert(0, str(ROOT))
+    import bench
+
+    for w in ("decode", "prefill", "decode70b", "engine-tiny", "engine-8b", "engine-tiny-replay",
+              "engine-8b-replay", "kv-ops", "swap"):  # fmt: skip
+        sys.argv = ["bench.py", "--workload", w, "--collective", "pull"]
+        args = bench.parse()
+        assert args.workload == w and args.steps > 0
+    assert bench.collective_for(bench.parse(), 1) == "none"
+    assert bench.collective_for(bench.parse(), 8) == "pull"
+
+
+def test_reference_arm_prints_one_json_line() -> None:
+    out = subprocess.run(
+        [sys.executable, str(ROOT / "bench.py"), "--impl", "reference", "--steps", "1",
+         "--warmup", "0", "--batch", "16"],
+        capture_output=True, text=True, timeout=600, cwd=str(ROOT),
+    )  # fmt: skip
+    assert out.returncode == 0, out.stderr[-2000:]
+    lines = [ln for ln in out.stdout.splitlines() if ln.strip()]
+    assert len(lines) == 1
+    line = json.loads(lines[0])
+    for key in ("metric", "value", "unit", "n_gpus", "steps", "warmup", "ms_per_step",
+                "higher_is_better", "config", "cpu_baseline", "e2e"):  # fmt: skip
+        assert key in line, key
+    assert line["impl"] == "reference" and line["cpu_baseline"]["kind"] == "port"
