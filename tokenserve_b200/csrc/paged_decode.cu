@@ -38,7 +38,7 @@ namespace {
 
 // Tuning knobs (compile-time).
 #ifndef TS_DECODE_WARPS
-#define TS_DECODE_WARPS 6  // independent warp pipelines per CTA (one CTA per SM)
+#define TS_DECODE_WARPS 8  // independent warp pipelines per CTA (one CTA per SM)
 #endif
 #ifndef TS_DECODE_PART_BLOCKS
 #define TS_DECODE_PART_BLOCKS 64  // largest work item, in blocks
@@ -47,7 +47,7 @@ namespace {
 #define TS_DECODE_STATIC_MAX_BLOCKS 64  // static split while a group's range is at most this
 #endif
 #ifndef TS_DECODE_STAGES_D128
-#define TS_DECODE_STAGES_D128 4  // ring stages per warp at head_dim 128
+#define TS_DECODE_STAGES_D128 3  // ring stages per warp at head_dim 128
 #endif
 #ifndef TS_DECODE_MIN_ITEMS_PER_WARP
 #define TS_DECODE_MIN_ITEMS_PER_WARP 2  // dynamic claiming: the item size gives every warp this many
