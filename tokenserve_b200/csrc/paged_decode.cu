@@ -99,6 +99,7 @@ struct DecodeArgs {
   // signals[r][signal_index] for every r < n_signals, after every CTA's output stores.
   int n_signals;
   int* const* signals;
+  int remote_out;  // 1: output rows were stored into other GPUs' memory (push exchange)
   int signal_index;
   unsigned epoch;
   const void* query;
@@ -476,6 +477,10 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
   // the plan is reused): everything below reads the plan, the tables, the query or the pool, so
   // wait until the grid before this one has completed and its writes are visible.
   ts::wait_prior_grid();
+  // A pull gather launched programmatically after this grid may now become resident: it only
+  // polls the ranks' epochs until this grid (and the peers') publish, and it waits for this
+  // grid to complete before it exits.
+  if (a.n_signals > 0 && !a.remote_out) ts::allow_dependents();
   if (a.reuse_plan) {
     // The plan must have been made for this batch, head count, table width and grid.
     if (__ldg(a.header + 6) != a.batch || __ldg(a.header + 7) != a.num_kv_heads ||
@@ -983,9 +988,15 @@ __global__ void __launch_bounds__(kWarps * 32, 1)
   // system-wide before its CTA counts itself done; the last CTA then publishes the epoch to
   // every rank. The last CTA also re-zeroes the claim counter and this counter: every CTA has
   // stopped claiming, and the next launch on the stream may reuse the plan.
-  if (a.n_signals > 0) __threadfence_system();
+  // Before the CTA counts itself done, its output stores must be ordered before the last CTA's
+  // system-scope release of the epoch. Stores into another GPU's memory (push) are fenced at
+  // system scope by every thread; local stores (pull) only need the CTA barrier and one
+  // GPU-scope fence by the counting thread, whose release chain (fence, done counter, the last
+  // CTA's fence.sc.sys and st.release.sys) covers the whole CTA's writes.
+  if (a.n_signals > 0 && a.remote_out) __threadfence_system();
   __syncthreads();
   if (threadIdx.x == 0) {
+    if (a.n_signals > 0 && !a.remote_out) __threadfence();
     const int done = atomicAdd(a.header + 4, 1);
     if (done == int(gridDim.x) - 1) {
       if (a.n_signals > 0) {
@@ -1206,6 +1217,7 @@ int paged_decode_call(void* out, const void* query, int64_t query_token_stride,
   a.out_row_stride = int64_t(num_q_heads) * head_dim;
   a.out_head0 = 0;
   a.n_signals = 0;
+  a.remote_out = 0;
   a.signals = nullptr;
   a.signal_index = 0;
   a.epoch = 0;
@@ -1375,6 +1387,7 @@ extern "C" int ts_paged_decode_no_alloc(void* out, const void* query, int64_t qu
   a.out_row_stride = int64_t(num_q_heads) * head_dim;
   a.out_head0 = 0;
   a.n_signals = 0;
+  a.remote_out = 0;
   a.signals = nullptr;
   a.signal_index = 0;
   a.epoch = 0;
@@ -1499,6 +1512,7 @@ int paged_decode_exchange(bool pull, void* const* dst_outs, int32_t world, int32
   a.out_row_stride = int64_t(world) * num_q_heads * head_dim;
   a.out_head0 = rank * num_q_heads;
   a.n_signals = world;
+  a.remote_out = pull ? 0 : 1;
   a.signals = reinterpret_cast<int* const*>(signals);
   a.signal_index = rank;
   a.epoch = epoch;
@@ -1598,7 +1612,10 @@ __global__ void __launch_bounds__(256) gather_peers_kernel(uint8_t* const* fulls
     }
   }
   __syncthreads();
-  if (!ready) return;
+  if (!ready) {
+    ts::wait_prior_grid();
+    return;
+  }
   uint8_t* mine = fulls[rank];
   const int64_t chunks = slice_bytes / 16;        // per row of one rank
   const int64_t per_rank = int64_t(batch) * chunks;
@@ -1612,6 +1629,9 @@ __global__ void __launch_bounds__(256) gather_peers_kernel(uint8_t* const* fulls
     const int64_t off = b * row_bytes + int64_t(r) * slice_bytes + k * 16;
     *reinterpret_cast<uint4*>(mine + off) = *reinterpret_cast<const uint4*>(fulls[r] + off);
   }
+  // Launched programmatically, this grid may have started before the decode grid before it
+  // finished; it completes only after that grid has, so later work on the stream sees both.
+  ts::wait_prior_grid();
 }
 
 extern "C" int ts_gather_peers(void* const* fulls, int32_t world, int32_t rank,
@@ -1630,10 +1650,22 @@ extern "C" int ts_gather_peers(void* const* fulls, int32_t world, int32_t rank,
                          "gather_peers: fulls and signals must be in the current device's memory");
   const int64_t chunks = int64_t(world - 1) * batch * (slice_bytes / 16);
   const int grid = int(std::max<int64_t>(1, std::min<int64_t>(2 * num_sms(), (chunks + 255) / 256)));
-  gather_peers_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(
-      reinterpret_cast<uint8_t* const*>(fulls), world, rank,
-      reinterpret_cast<const int*>(local_signals), epoch, batch, slice_bytes * world, slice_bytes,
-      reinterpret_cast<int*>(status));
+  // Programmatic launch: resident (and polling) while the decode before it finishes.
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(256);
+  cfg.stream = static_cast<cudaStream_t>(stream);
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t e = cudaLaunchKernelEx(
+      &cfg, gather_peers_kernel, reinterpret_cast<uint8_t* const*>(fulls), int(world), int(rank),
+      reinterpret_cast<const int*>(local_signals), unsigned(epoch), int(batch),
+      int64_t(slice_bytes * world), int64_t(slice_bytes), reinterpret_cast<int*>(status));
+  if (e != cudaSuccess)
+    return ts::set_error(static_cast<int>(e), "gather_peers: launch: %s", cudaGetErrorString(e));
   return ts::launch_status("gather_peers");
 }
 
