@@ -30,6 +30,9 @@ def test_bench_parses_every_workload() -> None:
         assert args.workload == w and args.steps > 0
     assert bench.collective_for(bench.parse(), 1) == "none"
     assert bench.collective_for(bench.parse(), 8) == "pull"
+    sys.argv = ["bench.py"]
+    assert bench.collective_for(bench.parse(), 2) == "nccl"
+    assert bench.collective_for(bench.parse(), 4) == "pull"
 
 
 def test_reference_arm_prints_one_json_line() -> None:
