@@ -27,9 +27,11 @@ from tokenserve_b200.workloads import small_paged_case
 pytestmark = pytest.mark.gpu
 
 
-def _peer_call(lib, dst, world, rank, sig, epoch, q, kp, vp, bt, cl, scale, ws, reuse=0):  # type: ignore[no-untyped-def]
+def _peer_call(lib, dst, world, rank, sig, epoch, q, kp, vp, bt, cl, scale, ws, reuse=0,  # type: ignore[no-untyped-def]
+               pull=False):  # fmt: skip
     nb, hkv, bs, d = kp.shape
-    code = lib.ts_paged_decode_peer(
+    fn = lib.ts_paged_decode_publish if pull else lib.ts_paged_decode_peer
+    code = fn(
         dst.data_ptr(), world, rank, sig.data_ptr(), epoch, q.data_ptr(), q.stride(0),
         kp.data_ptr(), vp.data_ptr(), bt.data_ptr(), bt.shape[1], cl.data_ptr(), q.shape[0],
         q.shape[1], hkv, d, bs, nb, scale, ops.TS_BFLOAT16, ws.data_ptr(),
@@ -134,6 +136,76 @@ def test_peer_decode_reuses_the_plan_across_layers(cuda_device) -> None:  # type
         for ws in wss:  # claim and CTA counters back at zero, no error
             h = ws[:20].view(torch.int32).tolist()
             assert h[0] == 0 and h[1] == 0 and h[4] == 0
+
+
+def test_pull_exchange_of_two_ranks_on_one_gpu(cuda_device) -> None:  # type: ignore[no-untyped-def]
+    """Both ranks' publish decodes run first (neither waits on anything), then each rank's
+    gather, whose waits are already satisfied: every buffer ends up equal to the ranks' own
+    decodes side by side, and each rank's decode wrote only its own buffer."""
+    lib = ops.load_library()
+    hq, hkv, d, world = 16, 4, 128, 2
+    ctx = [1, 0, 17, 300, 1500, 4000, 64, 999]
+    case = small_paged_case(7, ctx, num_q_heads=hq, num_kv_heads=hkv, head_dim=d)
+    g = torch.Generator().manual_seed(3)
+    shape = (case.num_blocks, hkv, 16, d)
+    kp = (torch.randn(shape, generator=g) * 0.5).to(torch.bfloat16)
+    vp = (torch.randn(shape, generator=g) * 0.5).to(torch.bfloat16)
+    q = (torch.randn(case.batch, hq, d, generator=g) * 0.5).to(torch.bfloat16)
+    bt = torch.from_numpy(case.block_tables).to(cuda_device)
+    cl = torch.from_numpy(case.context_lens).to(cuda_device)
+    full = [torch.full((case.batch, hq, d), 7.0, dtype=torch.bfloat16, device=cuda_device)
+            for _ in range(world)]  # fmt: skip
+    sigs = [torch.zeros(world, dtype=torch.int32, device=cuda_device) for _ in range(world)]
+    dst = torch.tensor([f.data_ptr() for f in full], dtype=torch.int64, device=cuda_device)
+    sig = torch.tensor([s_.data_ptr() for s_ in sigs], dtype=torch.int64, device=cuda_device)
+    plain = []
+    for r in range(world):
+        sh = shard_heads(hq, hkv, world, r)
+        kr, vr = shard_pool(kp, sh).to(cuda_device), shard_pool(vp, sh).to(cuda_device)
+        qr = q[:, sh.q_slice].contiguous().to(cuda_device)
+        ws = torch.empty(ops.decode_workspace_size(case.batch, sh.num_q_heads, sh.num_kv_heads, d,
+                                                   bt.shape[1], 16, torch.bfloat16),
+                         dtype=torch.uint8, device=cuda_device)  # fmt: skip
+        _peer_call(lib, dst, world, r, sig, 1, qr, kr, vr, bt, cl, d**-0.5, ws, pull=True)
+        out = torch.empty_like(qr)
+        ops.paged_decode(out, qr, kr, vr, bt, cl, d**-0.5, ws)
+        plain.append(out)
+    torch.cuda.synchronize()
+    for r in range(world):  # before the gathers: each buffer holds only its own rank's rows
+        own = slice(r * hq // world, (r + 1) * hq // world)
+        assert torch.equal(full[r][:, own], plain[r])
+        other = [h for h in range(hq) if not own.start <= h < own.stop]
+        assert bool((full[r][:, other] == 7.0).all())
+    status = torch.zeros(1, dtype=torch.int32, device=cuda_device)
+    for r in range(world):
+        assert lib.ts_gather_peers(dst.data_ptr(), world, r, sigs[r].data_ptr(), 1, case.batch,
+                                   hq // world, d, ops.TS_BFLOAT16, status.data_ptr(),
+                                   torch.cuda.current_stream().cuda_stream) == 0  # fmt: skip
+    torch.cuda.synchronize()
+    assert int(status) == 0
+    expect = torch.cat(plain, dim=1)
+    for f in full:
+        assert torch.equal(f, expect)
+
+
+def test_gather_for_an_unpublished_epoch_times_out(cuda_device) -> None:  # type: ignore[no-untyped-def]
+    """A rank that never publishes: the gather gives up after its bounded wait, copies nothing
+    and reports status 3; the context stays usable."""
+    lib = ops.load_library()
+    world, b, h, d = 2, 4, 2, 128
+    full = [torch.full((b, world * h, d), float(r + 1), dtype=torch.bfloat16, device=cuda_device)
+            for r in range(world)]  # fmt: skip
+    dst = torch.tensor([f.data_ptr() for f in full], dtype=torch.int64, device=cuda_device)
+    sigs = torch.tensor([5, 1], dtype=torch.int32, device=cuda_device)  # rank 1 is behind
+    status = torch.zeros(1, dtype=torch.int32, device=cuda_device)
+    assert lib.ts_gather_peers(dst.data_ptr(), world, 0, sigs.data_ptr(), 5, b, h, d,
+                               ops.TS_BFLOAT16, status.data_ptr(),
+                               torch.cuda.current_stream().cuda_stream) == 0  # fmt: skip
+    torch.cuda.synchronize()
+    assert int(status) == 3
+    assert bool((full[0] == 1.0).all())  # nothing was copied
+    x = torch.ones(4, device=cuda_device)
+    assert float((x * 2).sum()) == 8.0
 
 
 def test_wait_for_an_unpublished_epoch_times_out(cuda_device) -> None:  # type: ignore[no-untyped-def]
