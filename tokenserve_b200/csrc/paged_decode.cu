@@ -1594,6 +1594,11 @@ __global__ void __launch_bounds__(256) gather_peers_kernel(uint8_t* const* fulls
                                                            unsigned epoch, int batch,
                                                            int64_t row_bytes, int64_t slice_bytes,
                                                            int* status) {
+  // Launched programmatically, the grid is resident while this rank's decode still runs, but it
+  // polls nothing until that grid has completed: hundreds of CTAs polling the signal words would
+  // keep one L2 slice busy under the decode's own traffic. Completing after it, this grid also
+  // orders later work on the stream behind both.
+  ts::wait_prior_grid();
   __shared__ int ready;
   if (threadIdx.x == 0) ready = 1;
   __syncthreads();
@@ -1612,10 +1617,7 @@ __global__ void __launch_bounds__(256) gather_peers_kernel(uint8_t* const* fulls
     }
   }
   __syncthreads();
-  if (!ready) {
-    ts::wait_prior_grid();
-    return;
-  }
+  if (!ready) return;
   uint8_t* mine = fulls[rank];
   const int64_t chunks = slice_bytes / 16;        // per row of one rank
   const int64_t per_rank = int64_t(batch) * chunks;
@@ -1629,9 +1631,6 @@ __global__ void __launch_bounds__(256) gather_peers_kernel(uint8_t* const* fulls
     const int64_t off = b * row_bytes + int64_t(r) * slice_bytes + k * 16;
     *reinterpret_cast<uint4*>(mine + off) = *reinterpret_cast<const uint4*>(fulls[r] + off);
   }
-  // Launched programmatically, this grid may have started before the decode grid before it
-  // finished; it completes only after that grid has, so later work on the stream sees both.
-  ts::wait_prior_grid();
 }
 
 extern "C" int ts_gather_peers(void* const* fulls, int32_t world, int32_t rank,
@@ -1650,7 +1649,7 @@ extern "C" int ts_gather_peers(void* const* fulls, int32_t world, int32_t rank,
                          "gather_peers: fulls and signals must be in the current device's memory");
   const int64_t chunks = int64_t(world - 1) * batch * (slice_bytes / 16);
   const int grid = int(std::max<int64_t>(1, std::min<int64_t>(2 * num_sms(), (chunks + 255) / 256)));
-  // Programmatic launch: resident (and polling) while the decode before it finishes.
+  // Programmatic launch: resident (its launch latency hidden) while the decode before it finishes.
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
