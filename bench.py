@@ -215,6 +215,16 @@ def cpu_rate(case, seqs, ks, vs, qs, seconds_target, threads):  # type: ignore[n
 # ----------------------------------------------------------------------------- clocks
 
 
+def settle_host() -> None:
+    """Collects garbage and freezes the surviving objects before a timed region, so that a
+    full collection over the bench's earlier allocations cannot land inside it (as a server
+    does once its start-up is done)."""
+    import gc
+
+    gc.collect()
+    gc.freeze()
+
+
 class ClockSampler:
     """Polls SM clock, power and clock-event reasons through NVML while the timed region runs.
 
@@ -269,6 +279,7 @@ class ClockSampler:
     def __enter__(self) -> ClockSampler:
         import threading
 
+        settle_host()
         try:
             import pynvml
 
@@ -409,6 +420,7 @@ def run_reference(args: argparse.Namespace, world: int) -> None:
     sample_bytes = sum(int(case.context_lens[b]) for b in seqs) * per_tok
     for _ in range(args.warmup):
         cpu_sample(case, ks, vs, qs, seqs, threads)
+    settle_host()
     times = [cpu_sample(case, ks, vs, qs, seqs, threads) for _ in range(args.steps)]
     total = sum(times)
     gbs = sample_bytes * args.steps / total / 1e9
@@ -693,9 +705,13 @@ def run_cuda(args: argparse.Namespace, world: int, rank: int, local: int) -> dic
     # ---- end to end through the C-ABI with host buffers
     # Every step copies its inputs from pinned host memory and its attention output (the full
     # [B, 32, D] at N>1) back to the host. As a serving loop would, the copies run on their own
-    # streams with two buffer sets, so step i+1's upload and step i-1's download overlap step
-    # i's kernels. A step's six inputs sit in one pinned host buffer (256-byte aligned
-    # sections) and go up with ONE copy into the matching device buffer.
+    # streams with three buffer sets and the host reads step i-2's result while step i runs:
+    # the uploads and downloads overlap the kernels, and a step's upload waits for the download
+    # of the step that last used its buffers, not for the one before it (with two sets, that
+    # chain of PCIe copies and host wake-ups, ~0.3 ms, sat inside a two-step cycle). A step's
+    # six inputs sit in one pinned host buffer (256-byte aligned sections) and go up with ONE
+    # copy into the matching device buffer.
+    ring = 3
     srcs = (q, knew, vnew, slots, bt, cl)
     offs, o = [], 0
     for t in srcs:
@@ -709,28 +725,29 @@ def run_cuda(args: argparse.Namespace, world: int, rank: int, local: int) -> dic
 
     for dst, src in zip(views(h_buf), srcs, strict=True):
         dst.copy_(src.cpu())
-    d_buf = [torch.empty(o, dtype=torch.uint8, device=dev) for _ in range(2)]
+    d_buf = [torch.empty(o, dtype=torch.uint8, device=dev) for _ in range(ring)]
     d_in = [views(b) for b in d_buf]
     out_shape = (B, hq * world, d)
-    h_out = [torch.empty(out_shape, dtype=dt).pin_memory() for _ in range(2)]
-    d_out = [torch.empty(out_shape, dtype=dt, device=dev) for _ in range(2)]
+    h_out = [torch.empty(out_shape, dtype=dt).pin_memory() for _ in range(ring)]
+    d_out = [torch.empty(out_shape, dtype=dt, device=dev) for _ in range(ring)]
     h2d = o  # the packed buffer: the six inputs plus alignment padding
     d2h = h_out[0].numel() * h_out[0].element_size()
     up, down = torch.cuda.Stream(device=dev), torch.cuda.Stream(device=dev)
-    uploaded = [torch.cuda.Event() for _ in range(2)]
-    computed = [torch.cuda.Event() for _ in range(2)]
-    fetched = [torch.cuda.Event() for _ in range(2)]
+    uploaded = [torch.cuda.Event() for _ in range(ring)]
+    computed = [torch.cuda.Event() for _ in range(ring)]
+    fetched = [torch.cuda.Event() for _ in range(ring)]
+
     def e2e_run(n: int) -> None:
         for i in range(n):
-            p = i % 2
+            p = i % ring
             with torch.cuda.stream(up):
-                if i >= 2:
-                    up.wait_event(computed[p])  # step i-2 is done reading d_in[p]
+                if i >= ring:
+                    up.wait_event(computed[p])  # step i-3 is done reading d_in[p]
                 d_buf[p].copy_(h_buf, non_blocking=True)
                 uploaded[p].record(up)
             stream.wait_event(uploaded[p])
-            if i >= 2:
-                stream.wait_event(fetched[p])  # step i-2's output has left d_out[p]
+            if i >= ring:
+                stream.wait_event(fetched[p])  # step i-3's output has left d_out[p]
             dq, dk, dv, ds, dbt, dcl = d_in[p]
             ops.reshape_and_cache(dk, dv, kpool, vpool, ds)
             if world == 1:
@@ -747,11 +764,12 @@ def run_cuda(args: argparse.Namespace, world: int, rank: int, local: int) -> dic
                 down.wait_event(computed[p])
                 h_out[p].copy_(d_out[p], non_blocking=True)
                 fetched[p].record(down)
-            if i >= 1:
-                fetched[(i - 1) % 2].synchronize()  # the host reads step i-1's result
+            if i >= ring - 1:
+                fetched[(i - ring + 1) % ring].synchronize()  # the host reads step i-2's result
         torch.cuda.synchronize()
 
     e2e_run(max(args.warmup, 3))
+    settle_host()
     barrier()
     t_e2e = time.perf_counter()
     e2e_run(args.steps)
@@ -845,7 +863,8 @@ def run_cuda(args: argparse.Namespace, world: int, rank: int, local: int) -> dic
                 "d2h_bytes_per_step": d2h,
                 "ms_per_step": round(1000 * e2e_elapsed / args.steps, 4),
                 "timing": "host wall clock from the first upload to the last result on the "
-                          "host; uploads and downloads double-buffered on two copy streams",
+                          "host; uploads and downloads on two copy streams with three buffer "
+                          "sets, the host reading step i-2's result while step i runs",
             },
             # K1, the decode's prep kernel and the decode (+ the peer-wait kernel when fused)
             "gpu_launches": launches * args.steps,
@@ -1297,6 +1316,7 @@ def engine_tiny_live(dev, cpu_baseline: bool, cpu_seconds: float) -> dict:  # ty
         n = len(reqs)
         # Bounded: the first requests only when the host is slow (~cpu_seconds of work).
         sub = type(reqs)(reqs.prompts[:n], reqs.max_tokens[:n], reqs.arrivals[:n])
+        settle_host()
         rc = drive_engine(HFBackend(build_model("engine-tiny", "cpu")), sub, block_size=16,
                           num_blocks=512, open_loop=False)  # fmt: skip
         cmism = sum(a != b for i, toks in rc["tokens"].items()
