@@ -80,8 +80,8 @@ def parse() -> argparse.Namespace:
                          "its rows into every rank's buffer over NVLink), pull (the decode writes "
                          "its own buffer and publishes; a gather kernel then reads the other "
                          "ranks' rows over NVLink), nccl (all-gather on a second stream); auto: "
-                         "NCCL at 2 ranks and pull above for the decode op, fused below 8 "
-                         "ranks and NCCL at 8 for decode70b")  # fmt: skip
+                         "pull for the decode op, fused below 8 ranks and NCCL at 8 for "
+                         "decode70b")  # fmt: skip
     ap.add_argument("--resident-layers", type=int, default=0,
                     help="decode70b: layer pools kept resident (0 = as many as fit); layers "
                          "cycle through them, each still read in full from HBM")  # fmt: skip
@@ -151,10 +151,11 @@ def collective_for(args: argparse.Namespace, world: int) -> str:
         return "none"
     if args.collective != "auto":
         return args.collective
-    # Measured on this workload: at 2 ranks NCCL's all-gather on a second stream (0.181 ms per
-    # step) beats pull (0.192) and fused (0.196); from 4 ranks the persistent decode loses SMs
-    # to NCCL's kernels and the push form's remote stores slow the decode, so pull is used.
-    return "nccl" if world == 2 else "pull"
+    # Measured on this workload: pull is the fastest exchange from 4 ranks (the persistent decode
+    # loses SMs to NCCL's kernels, and the push form's remote stores slow the decode). At 2 ranks
+    # its device step ties NCCL's (0.177-0.186 ms against 0.176-0.178) and its end-to-end rate
+    # is 13% higher (9.3 against 8.1-8.3 TB/s: the download need not wait for a second stream).
+    return "pull"
 
 
 # ----------------------------------------------------------------------------- CPU side

@@ -31,7 +31,7 @@ def test_bench_parses_every_workload() -> None:
     assert bench.collective_for(bench.parse(), 1) == "none"
     assert bench.collective_for(bench.parse(), 8) == "pull"
     sys.argv = ["bench.py"]
-    assert bench.collective_for(bench.parse(), 2) == "nccl"
+    assert bench.collective_for(bench.parse(), 2) == "pull"
     assert bench.collective_for(bench.parse(), 4) == "pull"
 
 
