@@ -161,22 +161,55 @@ def collective_for(args: argparse.Namespace, world: int) -> str:
 # ----------------------------------------------------------------------------- CPU side
 
 
-def cpu_sample(case, k_host, v_host, q_host, seqs, threads):  # type: ignore[no-untyped-def]
-    """One pass of the oracle over `seqs` (a bounded sample); returns seconds."""
-    import torch
+def reference_attention(num_q_heads: int, num_kv_heads: int):  # type: ignore[no-untyped-def]
+    """The attention HFBackend's Llama runs, transformers 5.5.0 ``eager_attention_forward``
+    (models/llama/modeling_llama.py:199), as ``f(q [1, Hq, n, D], k/v [1, Hkv, S, D], mask,
+    scale)``, with its kind for ``cpu_baseline``: "reference" when transformers imports, else
+    the oracle's restatement of the same steps ("port")."""
+    import types
 
-    from oracle.attention import eager_attention_torch
+    try:
+        from transformers.models.llama.modeling_llama import eager_attention_forward
+    except ImportError:
+        from oracle.attention import eager_attention_torch
 
-    torch.set_num_threads(threads)
-    bs = case.block_size
-    t0 = time.perf_counter()
+        def port(q, k, v, mask, scale):  # type: ignore[no-untyped-def]
+            return eager_attention_torch(q[0], k[0], v[0], scale, causal=mask is not None)
+
+        return port, "port", "the oracle's float32 restatement of eager attention"
+    module = types.SimpleNamespace(num_key_value_groups=num_q_heads // num_kv_heads,
+                                   training=False)  # fmt: skip
+
+    def ref(q, k, v, mask, scale):  # type: ignore[no-untyped-def]
+        return eager_attention_forward(module, q, k, v, mask, scale)[0]
+
+    return ref, "reference", "transformers 5.5.0 eager_attention_forward (what HFBackend's Llama runs)"
+
+
+def cpu_inputs(case, k_host, v_host, q_host, seqs):  # type: ignore[no-untyped-def]
+    """The sample as HFBackend holds it: per sequence a float32 query [1, Hq, 1, D] and a
+    contiguous float32 KV cache [1, Hkv, ctx, D] (its per-sequence past_key_values), made once
+    before any timing."""
+    bs, hkv, d = case.block_size, case.num_kv_heads, case.head_dim
+    out = []
     for i, b in enumerate(seqs):
         ctx = int(case.context_lens[b])
         nblk = (ctx + bs - 1) // bs
-        k = k_host[i][:, :nblk].reshape(case.num_kv_heads, nblk * bs, case.head_dim)[:, :ctx]
-        v = v_host[i][:, :nblk].reshape(case.num_kv_heads, nblk * bs, case.head_dim)[:, :ctx]
-        eager_attention_torch(q_host[i][:, None, :].float(), k.float(), v.float(),
-                              case.head_dim**-0.5, causal=False)  # fmt: skip
+        k = k_host[i][:, :nblk].reshape(hkv, nblk * bs, d)[:, :ctx].float().contiguous()[None]
+        v = v_host[i][:, :nblk].reshape(hkv, nblk * bs, d)[:, :ctx].float().contiguous()[None]
+        out.append((q_host[i].float()[None, :, None, :].contiguous(), k, v))
+    return out
+
+
+def cpu_sample(case, inputs, threads, attend):  # type: ignore[no-untyped-def]
+    """One pass of the reference's attention over a bounded sample; returns seconds."""
+    import torch
+
+    torch.set_num_threads(threads)
+    scale = case.head_dim**-0.5
+    t0 = time.perf_counter()
+    for q, k, v in inputs:
+        attend(q, k, v, None, scale)
     return time.perf_counter() - t0
 
 
@@ -204,13 +237,18 @@ def gather_sample(case, kpool, vpool, q, budget_bytes):  # type: ignore[no-untyp
 
 
 def cpu_rate(case, seqs, ks, vs, qs, seconds_target, threads):  # type: ignore[no-untyped-def]
-    """KV GB/s of the oracle on the sample, timed over repeats filling ~seconds_target."""
+    """KV GB/s (of the bf16 KV the workload reads) of the reference's attention on the sample,
+    timed over repeats filling ~seconds_target; also the sample's bytes, the repeats and the
+    kind and name of what ran."""
     per_tok = case.num_kv_heads * case.head_dim * 2 * 2
     sample_bytes = sum(int(case.context_lens[b]) for b in seqs) * per_tok
-    t1 = cpu_sample(case, ks, vs, qs, seqs, threads)
+    attend, kind, what = reference_attention(case.num_q_heads, case.num_kv_heads)
+    inputs = cpu_inputs(case, ks, vs, qs, seqs)
+    t1 = cpu_sample(case, inputs, threads, attend)
     reps = max(1, int(seconds_target / max(t1, 1e-3)))
-    t = sum(cpu_sample(case, ks, vs, qs, seqs, threads) for _ in range(reps))
-    return sample_bytes * reps / t / 1e9, sample_bytes, reps
+    settle_host()
+    t = sum(cpu_sample(case, inputs, threads, attend) for _ in range(reps))
+    return sample_bytes * reps / t / 1e9, sample_bytes, reps, kind, what
 
 
 # ----------------------------------------------------------------------------- clocks
@@ -395,7 +433,9 @@ def prefill_extra(args: argparse.Namespace, dev) -> dict:  # type: ignore[no-unt
 
 
 def run_reference(args: argparse.Namespace, world: int) -> None:
-    """CPU oracle on the box's host cores, on a bounded sample of each step's workload."""
+    """The reference's attention on the box's host cores (transformers' eager_attention_forward,
+    which HFBackend's Llama runs; the oracle's restatement if transformers does not import), on
+    a bounded sample of each step's workload."""
     import torch
 
     from tokenserve_b200.workloads import decode_workload
@@ -419,13 +459,16 @@ def run_reference(args: argparse.Namespace, world: int) -> None:
         if used >= budget:
             break
     sample_bytes = sum(int(case.context_lens[b]) for b in seqs) * per_tok
+    attend, kind, what = reference_attention(case.num_q_heads, case.num_kv_heads)
+    inputs = cpu_inputs(case, ks, vs, qs, seqs)
     for _ in range(args.warmup):
-        cpu_sample(case, ks, vs, qs, seqs, threads)
+        cpu_sample(case, inputs, threads, attend)
     settle_host()
-    times = [cpu_sample(case, ks, vs, qs, seqs, threads) for _ in range(args.steps)]
+    times = [cpu_sample(case, inputs, threads, attend) for _ in range(args.steps)]
     total = sum(times)
     gbs = sample_bytes * args.steps / total / 1e9
-    sample = f"{len(seqs)} of {case.batch} sequences ({sample_bytes / 1e6:.0f} MB of KV) per step"
+    sample = (f"{len(seqs)} of {case.batch} sequences ({sample_bytes / 1e6:.0f} MB of bf16 KV) "
+              f"per step through {what}, float32, one sequence at a time as HFBackend runs them")
     print(json.dumps({
         "impl": "reference",
         "metric": METRIC,
@@ -442,7 +485,7 @@ def run_reference(args: argparse.Namespace, world: int) -> None:
         "data": "synthetic",
         "config": config(args, world),
         "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": threads,
-                         "kind": "port", "sample": sample},
+                         "kind": kind, "sample": sample},
         "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }))  # fmt: skip
@@ -889,13 +932,15 @@ def run_cuda(args: argparse.Namespace, world: int, rank: int, local: int) -> dic
         if world == 1 and not args.no_cpu_baseline:
             seqs, ks, vs, qs = gather_sample(case, kpool, vpool, q, 96 * 2**20)
             threads = os.cpu_count() or 1
-            gbs, sb, reps = cpu_rate(case, seqs, ks, vs, qs, args.cpu_sample_seconds, threads)
+            gbs, sb, reps, kind, what = cpu_rate(case, seqs, ks, vs, qs, args.cpu_sample_seconds,
+                                                 threads)  # fmt: skip
             line["cpu_baseline"] = {
                 "value": round(gbs, 3),
                 "unit": "GB/s",
                 "cores": threads,
-                "kind": "port",
-                "sample": f"{len(seqs)} of {B} sequences ({sb / 1e6:.0f} MB of KV) x {reps} passes",
+                "kind": kind,
+                "sample": f"{len(seqs)} of {B} sequences ({sb / 1e6:.0f} MB of bf16 KV, gathered "
+                          f"from the timed pools) x {reps} passes through {what}, float32",
             }
     if pg is not None:
         pg.close()
@@ -1646,16 +1691,17 @@ PREFILL_METRIC = "chunked-prefill paged attention TFLOP/s (bf16, % of tensor pea
 
 
 def prefill_cpu_rate(work, seconds_target, threads):  # type: ignore[no-untyped-def]
-    """Oracle TFLOP/s on sequence 0's chunks (one layer), repeated for ~seconds_target.
+    """The reference's attention in TFLOP/s on sequence 0's chunks (one layer), repeated for
+    ~seconds_target; also the FLOPs, the repeats and the kind of what ran.
 
-    The CPU times float32 eager attention over seeded host inputs of the workload's shapes
-    (the chunk's queries over the cached prefix plus the chunk), as HFBackend would compute it.
+    The CPU times float32 eager attention (``reference_attention``) over seeded host inputs of
+    the workload's shapes: the chunk's queries over the cached prefix plus the chunk, with the
+    additive causal mask transformers builds for a multi-token step.
     """
     import torch
 
-    from oracle.attention import eager_attention_torch
-
     torch.set_num_threads(threads)
+    attend, kind, _ = reference_attention(32, 8)
     g = torch.Generator().manual_seed(7)
     jobs = []
     for r in work.rounds:
@@ -1663,24 +1709,28 @@ def prefill_cpu_rate(work, seconds_target, threads):  # type: ignore[no-untyped-
             continue
         i = r.seqs.tolist().index(0)
         ctx, c = int(r.context_lens[i]), int(r.chunk_lens[i])
-        jobs.append((torch.randn(32, c, 128, generator=g) * 0.5,
-                     torch.randn(8, ctx, 128, generator=g) * 0.5,
-                     torch.randn(8, ctx, 128, generator=g) * 0.5))  # fmt: skip
+        # query row i sits at position ctx - c + i and sees keys 0 .. ctx - c + i
+        visible = torch.arange(ctx)[None, :] <= torch.arange(ctx - c, ctx)[:, None]
+        mask = torch.zeros(c, ctx).masked_fill(~visible, float("-inf"))[None, None]
+        jobs.append(((torch.randn(32, c, 128, generator=g) * 0.5)[None],
+                     (torch.randn(8, ctx, 128, generator=g) * 0.5)[None],
+                     (torch.randn(8, ctx, 128, generator=g) * 0.5)[None], mask))  # fmt: skip
     flops = 0
-    for qh, k, _ in jobs:
-        c, n_prev = qh.shape[1], k.shape[1] - qh.shape[1]
+    for qh, k, _, _ in jobs:
+        c, n_prev = qh.shape[2], k.shape[2] - qh.shape[2]
         flops += 4 * 32 * 128 * (c * n_prev + c * (c + 1) // 2)
 
     def once() -> float:
         t0 = time.perf_counter()
-        for qh, k, v in jobs:
-            eager_attention_torch(qh, k, v, 128**-0.5, causal=True)
+        for qh, k, v, mask in jobs:
+            attend(qh, k, v, mask, 128**-0.5)
         return time.perf_counter() - t0
 
     t1 = once()
     reps = max(1, int(seconds_target / max(t1, 1e-3)))
+    settle_host()
     t = sum(once() for _ in range(reps))
-    return flops * reps / t / 1e12, flops, reps
+    return flops * reps / t / 1e12, flops, reps, kind
 
 
 def prefill_measure(args: argparse.Namespace, dev, steps: int, warmup: int, seed: int = 0,
@@ -1857,9 +1907,10 @@ def run_prefill(args: argparse.Namespace, world: int, rank: int, local: int) -> 
             "clocks": res["clocks"].summary(),
         }  # fmt: skip
         if world == 1 and not args.no_cpu_baseline:
-            tf, fl, reps = prefill_cpu_rate(work, args.cpu_sample_seconds, os.cpu_count() or 1)
+            tf, fl, reps, kind = prefill_cpu_rate(work, args.cpu_sample_seconds,
+                                                  os.cpu_count() or 1)  # fmt: skip
             line["cpu_baseline"] = {"value": round(tf, 4), "unit": "TFLOP/s",
-                                    "cores": os.cpu_count() or 1, "kind": "port",
+                                    "cores": os.cpu_count() or 1, "kind": kind,
                                     "sample": f"sequence 0's chunks, one layer ({fl / 1e9:.1f} "
                                               f"GFLOP) x {reps} passes"}  # fmt: skip
         print(json.dumps(line), flush=True)

@@ -51,5 +51,6 @@ def test_default_decode_line_keeps_the_contract(cuda_device) -> None:  # type: i
     e2e = line["e2e"]
     assert e2e["value"] > 0 and e2e["h2d_bytes_per_step"] > 0 and e2e["d2h_bytes_per_step"] > 0
     assert line["gpu_launches"] == 3 * steps  # K1, prep, decode per step
-    assert line["cpu_baseline"]["cores"] >= 1 and line["cpu_baseline"]["kind"] == "port"
+    assert line["cpu_baseline"]["cores"] >= 1
+    assert line["cpu_baseline"]["kind"] in ("reference", "port")
     assert line["clocks"]["sm_max_mhz"] is None or line["clocks"]["sm_max_mhz"] > 0
