@@ -420,7 +420,7 @@ def add_extras(args: argparse.Namespace, line: dict, local: int) -> None:
 def prefill_extra(args: argparse.Namespace, dev) -> dict:  # type: ignore[no-untyped-def]
     steps = 5
     res = prefill_measure(args, dev, steps, 3, parity=True)
-    return {
+    out = {
         "metric": PREFILL_METRIC,
         "workload": "chunked prefill with prefix cache, Llama-3-8B attention (32q/8kv, D=128, "
                     "bf16, block 16): 64 sequences, 1024-token cached prefix, suffixes "
@@ -430,6 +430,15 @@ def prefill_extra(args: argparse.Namespace, dev) -> dict:  # type: ignore[no-unt
         "roofline": prefill_roofline(res, steps), "parity": res.get("parity"),
         "gpu_launches": 2 * res["launches"], "clocks": res["clocks"].summary(),
     }  # fmt: skip
+    if not args.no_cpu_baseline:
+        threads = os.cpu_count() or 1
+        tf, fl, reps, kind = prefill_cpu_rate(res["work"], min(args.cpu_sample_seconds, 5.0),
+                                              threads)  # fmt: skip
+        out["cpu_baseline"] = {"value": round(tf, 4), "unit": "TFLOP/s", "cores": threads,
+                               "kind": kind,
+                               "sample": f"sequence 0's chunks, one layer ({fl / 1e9:.1f} GFLOP) "
+                                         f"x {reps} passes"}  # fmt: skip
+    return out
 
 
 def run_reference(args: argparse.Namespace, world: int) -> None:
