@@ -676,7 +676,8 @@ def run_cuda(args: argparse.Namespace, world: int, rank: int, local: int) -> dic
     # ---- device-resident timing
     step_no = [0]  # steps run so far (the peer exchange's buffers rotate with it)
 
-    def steps(n: int, k1_ev=None, dec_ev=None, ex_ev=None):  # type: ignore[no-untyped-def]
+    def run_steps(n: int, k1_ev=None, dec_ev=None, ex_ev=None):  # type: ignore[no-untyped-def]
+        """n steps (K1 + decode + exchange); the events, when given, after each part."""
         res = None
         for i in range(n):
             ops.reshape_and_cache(knew, vnew, kpool, vpool, slots)
@@ -687,7 +688,7 @@ def run_cuda(args: argparse.Namespace, world: int, rank: int, local: int) -> dic
             step_no[0] += 1
         return res
 
-    steps(max(args.warmup, 3))
+    run_steps(max(args.warmup, 3))
     stream.wait_stream(comm)
     barrier()
     # The timed steps carry no events between their kernels: an event recorded between K1 and
@@ -697,7 +698,7 @@ def run_cuda(args: argparse.Namespace, world: int, rank: int, local: int) -> dic
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(dev) as clocks:
         e0.record(stream)
-        last = steps(args.steps)
+        last = run_steps(args.steps)
         stream.wait_stream(comm)
         e1.record(stream)
         torch.cuda.synchronize()
@@ -739,7 +740,7 @@ def run_cuda(args: argparse.Namespace, world: int, rank: int, local: int) -> dic
     n_ev = min(args.steps, 50)
     t_k1, t_dec, t_ex = ([torch.cuda.Event(enable_timing=True) for _ in range(n_ev)]
                          for _ in range(3))  # fmt: skip
-    steps(n_ev, t_k1, t_dec, t_ex if world > 1 else None)
+    run_steps(n_ev, t_k1, t_dec, t_ex if world > 1 else None)
     stream.wait_stream(comm)
     torch.cuda.synchronize()
     barrier()
