@@ -245,21 +245,51 @@ __device__ void prep_static(DecodeArgs& a, int* warp_sums, long long WB, int run
   }
   int total = 0;
   int runc = block_exclusive_scan(c, &total, warp_sums);
-  u = run0;
-  for (int i = 0; i < cnt; ++i) {
-    const int b = b0 + i;
-    a.chunk_prefix[b] = runc;
-    const int ctx = ctx_of(a, b), n = blocks_of(ctx);
-    int k = 0;
-    if (n > 0)
-      for_each_chunk(u, u + n, gsp, [&](int g, int gs, int lo, int hi) {
-        a.part_info[2 * (runc + k)] = make_int4(b, lo - u, hi - lo, k);
-        if (lo == gs) a.group_first[g] = runc + k;  // the partition that opens group g
-        ++k;
-      });
-    for (int m = 0; m < k; ++m) a.part_info[2 * (runc + m) + 1] = make_int4(runc, k, ctx, 0);
-    runc += k;
-    u += n;
+  if (B <= int(blockDim.x)) {
+    // One sequence per thread (b0 = thread, cnt <= 1). The partitions are written in parallel,
+    // thread t taking partitions t, t + T, ...: a long sequence's tens of partitions would
+    // otherwise be one thread's serial loop, the prep's critical path. Partition p belongs to
+    // the last sequence b with s_runc[b] <= p (binary search; empty sequences share the next
+    // one's prefix) and is its k-th, k = p - s_runc[b], covering group group_of(u_b) + k.
+    __shared__ int s_runc[kPrepThreads + 1], s_u[kPrepThreads], s_ctx[kPrepThreads];
+    if (cnt > 0) {
+      s_runc[b0] = runc;
+      s_u[b0] = run0;
+      s_ctx[b0] = ctx_of(a, b0);
+      a.chunk_prefix[b0] = runc;
+    }
+    if (threadIdx.x == 0) s_runc[B] = total;
+    __syncthreads();
+    for (int p = threadIdx.x; p < total; p += blockDim.x) {
+      int lo = 0, hi = B;  // s_runc[lo] <= p < s_runc[hi]
+      while (hi - lo > 1) {
+        const int mid = (lo + hi) >> 1;
+        if (s_runc[mid] <= p) lo = mid; else hi = mid;
+      }
+      const int b = lo, k = p - s_runc[b], ub = s_u[b], ctx = s_ctx[b];
+      const int g = gsp.group_of(ub) + k, gs = gsp.start(g);
+      const int blk_lo = max(ub, gs), blk_hi = min(ub + blocks_of(ctx), gsp.start(g + 1));
+      a.part_info[2 * p] = make_int4(b, blk_lo - ub, blk_hi - blk_lo, k);
+      a.part_info[2 * p + 1] = make_int4(s_runc[b], s_runc[b + 1] - s_runc[b], ctx, 0);
+      if (blk_lo == gs) a.group_first[g] = p;  // the partition that opens group g
+    }
+  } else {
+    u = run0;
+    for (int i = 0; i < cnt; ++i) {
+      const int b = b0 + i;
+      a.chunk_prefix[b] = runc;
+      const int ctx = ctx_of(a, b), n = blocks_of(ctx);
+      int k = 0;
+      if (n > 0)
+        for_each_chunk(u, u + n, gsp, [&](int g, int gs, int lo, int hi) {
+          a.part_info[2 * (runc + k)] = make_int4(b, lo - u, hi - lo, k);
+          if (lo == gs) a.group_first[g] = runc + k;  // the partition that opens group g
+          ++k;
+        });
+      for (int m = 0; m < k; ++m) a.part_info[2 * (runc + m) + 1] = make_int4(runc, k, ctx, 0);
+      runc += k;
+      u += n;
+    }
   }
   if (threadIdx.x == 0) {
     a.chunk_prefix[B] = total;
