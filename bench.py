@@ -246,22 +246,31 @@ def cpu_rate(case, seqs, ks, vs, qs, seconds_target, threads):  # type: ignore[n
     inputs = cpu_inputs(case, ks, vs, qs, seqs)
     t1 = cpu_sample(case, inputs, threads, attend)
     reps = max(1, int(seconds_target / max(t1, 1e-3)))
-    settle_host()
-    t = sum(cpu_sample(case, inputs, threads, attend) for _ in range(reps))
+    with quiet_host():
+        t = sum(cpu_sample(case, inputs, threads, attend) for _ in range(reps))
     return sample_bytes * reps / t / 1e9, sample_bytes, reps, kind, what
 
 
 # ----------------------------------------------------------------------------- clocks
 
 
-def settle_host() -> None:
-    """Collects garbage and freezes the surviving objects before a timed region, so that a
-    full collection over the bench's earlier allocations cannot land inside it (as a server
-    does once its start-up is done)."""
-    import gc
+class quiet_host:
+    """Around a timed region: collects garbage and freezes the surviving objects on entry, so
+    that no full collection over the bench's earlier allocations lands inside the region (as a
+    server does once its start-up is done), and unfreezes them on exit, so that cycles alive
+    during the region (a backend and the helpers that point back at it) are collected later."""
 
-    gc.collect()
-    gc.freeze()
+    def __enter__(self) -> quiet_host:
+        import gc
+
+        gc.collect()
+        gc.freeze()
+        return self
+
+    def __exit__(self, *exc: object) -> None:
+        import gc
+
+        gc.unfreeze()
 
 
 class ClockSampler:
@@ -318,7 +327,7 @@ class ClockSampler:
     def __enter__(self) -> ClockSampler:
         import threading
 
-        settle_host()
+        self._quiet = quiet_host().__enter__()
         try:
             import pynvml
 
@@ -334,6 +343,7 @@ class ClockSampler:
         self._stop = True
         if self._thread is not None:
             self._thread.join(timeout=5)
+        self._quiet.__exit__()
 
     def summary(self) -> dict | None:
         if not self.samples:
@@ -472,8 +482,8 @@ def run_reference(args: argparse.Namespace, world: int) -> None:
     inputs = cpu_inputs(case, ks, vs, qs, seqs)
     for _ in range(args.warmup):
         cpu_sample(case, inputs, threads, attend)
-    settle_host()
-    times = [cpu_sample(case, inputs, threads, attend) for _ in range(args.steps)]
+    with quiet_host():
+        times = [cpu_sample(case, inputs, threads, attend) for _ in range(args.steps)]
     total = sum(times)
     gbs = sample_bytes * args.steps / total / 1e9
     sample = (f"{len(seqs)} of {case.batch} sequences ({sample_bytes / 1e6:.0f} MB of bf16 KV) "
@@ -823,11 +833,11 @@ def run_cuda(args: argparse.Namespace, world: int, rank: int, local: int) -> dic
         torch.cuda.synchronize()
 
     e2e_run(max(args.warmup, 3))
-    settle_host()
-    barrier()
-    t_e2e = time.perf_counter()
-    e2e_run(args.steps)
-    e2e_elapsed = time.perf_counter() - t_e2e
+    with quiet_host():
+        barrier()
+        t_e2e = time.perf_counter()
+        e2e_run(args.steps)
+        e2e_elapsed = time.perf_counter() - t_e2e
     barrier()
     if pg is not None:
         try:
@@ -1372,9 +1382,9 @@ def engine_tiny_live(dev, cpu_baseline: bool, cpu_seconds: float) -> dict:  # ty
         n = len(reqs)
         # Bounded: the first requests only when the host is slow (~cpu_seconds of work).
         sub = type(reqs)(reqs.prompts[:n], reqs.max_tokens[:n], reqs.arrivals[:n])
-        settle_host()
-        rc = drive_engine(HFBackend(build_model("engine-tiny", "cpu")), sub, block_size=16,
-                          num_blocks=512, open_loop=False)  # fmt: skip
+        with quiet_host():
+            rc = drive_engine(HFBackend(build_model("engine-tiny", "cpu")), sub, block_size=16,
+                              num_blocks=512, open_loop=False)  # fmt: skip
         cmism = sum(a != b for i, toks in rc["tokens"].items()
                     for a, b in zip(toks, want[f"r{i}"], strict=True))  # fmt: skip
         out["cpu_baseline"] = {
@@ -1738,8 +1748,8 @@ def prefill_cpu_rate(work, seconds_target, threads):  # type: ignore[no-untyped-
 
     t1 = once()
     reps = max(1, int(seconds_target / max(t1, 1e-3)))
-    settle_host()
-    t = sum(once() for _ in range(reps))
+    with quiet_host():
+        t = sum(once() for _ in range(reps))
     return flops * reps / t / 1e12, flops, reps, kind
 
 
