@@ -51,3 +51,43 @@ def test_reference_arm_prints_one_json_line() -> None:
     # transformers' own eager attention (what HFBackend's Llama runs) when it imports
     assert line["impl"] == "reference" and line["cpu_baseline"]["kind"] in ("reference", "port")
     assert "eager" in line["cpu_baseline"]["sample"]
+
+
+def test_reference_attention_matches_the_oracle() -> None:
+    """The attention the CPU legs time (transformers' eager_attention_forward, called as HFBackend
+    runs it) gives the oracle's results on a decode row and on a causal chunk over a prefix."""
+    import torch
+
+    sys.path.insert(0, str(ROOT))
+    import bench
+    from oracle.attention import eager_attention_torch
+
+    attend, kind, _ = bench.reference_attention(32, 8)
+    assert kind in ("reference", "port")
+    g = torch.Generator().manual_seed(0)
+    q = torch.randn(1, 32, 1, 128, generator=g)
+    k, v = torch.randn(1, 8, 300, 128, generator=g), torch.randn(1, 8, 300, 128, generator=g)
+    got = attend(q, k, v, None, 128**-0.5)  # [1, 1, 32, 128]
+    assert torch.allclose(got[0], eager_attention_torch(q[0], k[0], v[0], 128**-0.5, causal=False),
+                          atol=1e-6, rtol=1e-5)  # fmt: skip
+    c, ctx = 20, 50
+    qc = torch.randn(1, 32, c, 128, generator=g)
+    kc, vc = torch.randn(1, 8, ctx, 128, generator=g), torch.randn(1, 8, ctx, 128, generator=g)
+    visible = torch.arange(ctx)[None, :] <= torch.arange(ctx - c, ctx)[:, None]
+    mask = torch.zeros(c, ctx).masked_fill(~visible, float("-inf"))[None, None]
+    got = attend(qc, kc, vc, mask, 128**-0.5)
+    ref = eager_attention_torch(qc[0], kc[0], vc[0], 128**-0.5, causal=True)
+    assert torch.allclose(got[0], ref, atol=1e-6, rtol=1e-5)
+
+
+def test_quiet_host_freezes_only_inside_the_region() -> None:
+    import gc
+
+    sys.path.insert(0, str(ROOT))
+    import bench
+
+    keep = [[i] for i in range(1000)]  # objects alive across the region
+    before = gc.get_freeze_count()
+    with bench.quiet_host():
+        assert gc.get_freeze_count() >= before + len(keep)
+    assert gc.get_freeze_count() < len(keep)  # the region's freeze is released
