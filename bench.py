@@ -700,13 +700,15 @@ def run_cuda(args: argparse.Namespace, world: int, rank: int, local: int) -> dic
 
     run_steps(max(args.warmup, 3))
     stream.wait_stream(comm)
-    barrier()
     # The timed steps carry no events between their kernels: an event recorded between K1 and
     # the prep kernel, or between the decode and the gather, would cut the programmatic launch
     # overlap of the two (about 7 us a step). Events at the step boundaries (before K1, a plain
     # launch) cut nothing; their spacing is the step's duration.
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(dev) as clocks:
+        # after the sampler's garbage collection, which takes each rank its own time: without
+        # this barrier the first exchange would wait for the slowest rank's collection
+        barrier()
         e0.record(stream)
         last = run_steps(args.steps)
         stream.wait_stream(comm)
@@ -1092,6 +1094,7 @@ def run_decode70b(args: argparse.Namespace, world: int, rank: int, local: int) -
     ag_ev = [mk() for _ in range(args.steps)]
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(dev) as clocks:
+        barrier()  # after the sampler's garbage collection, which takes each rank its own time
         e0.record(comp)
         for i in range(args.steps):
             step(dec_ev[i], ag_ev[i])
